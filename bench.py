@@ -1,0 +1,334 @@
+#!/usr/bin/env python
+"""Benchmark: DeepSeek-R1 MoE-layer tokens/s on B200 (libdsmoe).
+
+Default workload (N=1): one MoE layer at the DeepSeek-R1 shape, prefill
+T=4096 tokens, all 256 routed experts + the shared expert resident in HBM
+(11.3 GB FP8), seeded synthetic weights and activations (no checkpoint, no
+dataset). One "step" = one full ``moe_block`` forward.
+
+Printed JSON keys (one line, rank 0):
+  value      tokens/s over all ranks, inputs resident in HBM, CUDA-event timed
+  e2e        same metric through ``moe_block`` with the input copied from pinned
+             host memory and the output read back every step
+  roofline   the dominant kernel (grouped gate/up GEMM): algorithmic bytes per
+             launch / its event-timed duration, against the measured HBM peak
+  cpu_baseline  the CPU oracle (a restatement of the reference's per-token
+             moe_block) timed on a bounded token sample on this host
+``--impl reference`` times only that CPU path and prints its own line.
+With N > 1 every rank runs its own replica of the layer (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "deepseek-on-one-gpu_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "MoE-layer tokens/s (DeepSeek-R1 FP8 shape) at 1/2/4/8 B200; % of FP8 TC peak"
+UNIT = "tokens/s"
+H, F, E, TOPK = 7168, 2048, 256, 8
+LAYER = 3
+FP8_DENSE_NOMINAL_TFLOPS = 4500.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in csv.reader(io.StringIO(out)):
+            if len(row) < 9:
+                continue
+            try:
+                idx = int(row[0])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            try:
+                sm.append(float(row[1]))
+                mx.append(float(row[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, row[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample(x_cpu, gate_cpu, get_expert, shared, budget_s: float, max_tokens: int):
+    """Time the oracle's per-token restatement of the reference's moe_block on
+    as many tokens as fit in ~budget_s (at least one)."""
+    from oracle import moe_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    O.moe_block_literal(x_cpu[:1].view(1, 1, -1), gate_cpu, get_expert, shared)  # warm (dequant, threads)
+    done, t0 = 0, time.perf_counter()
+    while done < max_tokens:
+        O.moe_block_literal(x_cpu[done:done + 1].view(1, 1, -1), gate_cpu, get_expert, shared)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, done, dt
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from dsmoe.synthetic import SyntheticLayer, activations
+
+    T = args.tokens
+    L = SyntheticLayer(1, LAYER, H, F, E, "cpu", cache=True)
+    x = activations(1, T, H)
+    torch.set_num_threads(os.cpu_count() or 1)
+    from oracle import moe_oracle as O
+
+    sample = x[: args.ref_tokens_per_step].view(1, -1, H)
+    for _ in range(args.warmup):
+        O.moe_block_literal(sample, L.gate, L.expert, L.shared())
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.moe_block_literal(sample, L.gate, L.expert, L.shared())
+    dt = time.perf_counter() - t0
+    n = args.steps * sample.shape[1]
+    v = n / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+        "config": {"workload": f"1 MoE layer, prefill T={T} (config 2 shape), per-token reference loop",
+                   "tokens_per_step_sample": sample.shape[1], "extrapolated": True},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{n} tokens of the T={T} batch through the oracle's per-token restatement of "
+                                   f"moe_block (inference/forward.py:112-153); tokens/s is linear in T"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="dsmoe", choices=["dsmoe", "reference"])
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--cpu-budget-s", type=float, default=15.0)
+    ap.add_argument("--ref-tokens-per-step", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from dsmoe import DeepSeekConfig, GPUTransfer, SyntheticWeightStore, moe_block
+    from dsmoe._lib import Workspace, set_profile_events
+    from dsmoe.synthetic import activations
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    T = args.tokens
+    cfg = DeepSeekConfig()
+    store = SyntheticWeightStore(cfg, seed=1 + rank, device=dev, pin_memory=False, gen_device="cuda")
+    gt = GPUTransfer(cfg, store, dev)
+    bank = gt.bank(LAYER)
+    x = activations(1 + rank, T, H, device=dev)
+
+    def step(inp):
+        return moe_block(inp, LAYER, store, gt, cfg)
+
+    # ---------------------------------------------------------- device-timed
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    sampler = ClockSampler({local} if world == 1 else set(range(world)))
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.5)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(x)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * T / (ms_max / 1000.0)
+
+    # ------------------------------------------------- per-stage (roofline)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    set_profile_events(evs)
+    stage_ms = [0.0] * 5
+    n_prof = max(3, args.steps // 2)
+    for _ in range(n_prof):
+        out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)
+        torch.cuda.synchronize()
+        for i in range(5):
+            stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
+    set_profile_events(None)
+    counts = torch.bincount(idx.reshape(-1), minlength=E).cpu()
+    touched = int((counts > 0).sum()) + 1  # + shared expert
+    rows = T * TOPK + T
+    w13 = 2 * F * H + 2 * (F // 128) * (H // 128) * 4
+    w2 = F * H + (F // 128) * (H // 128) * 4
+    gateup_bytes = touched * w13 + rows * H * 2 + rows * (H // 128) * 4 + rows * F * 2 + rows * (F // 128) * 4
+    down_bytes = touched * w2 + rows * F * 2 + rows * (F // 128) * 4 + rows * H * 2
+    algo_flops = 2.0 * rows * 3 * F * H  # useful FP8-GEMM work (hi/lo doubles what the tensor pipe executes)
+    hbm_peak, bf16_peak, peak_src = peaks()
+    gu_ms, dn_ms = stage_ms[2], stage_ms[3]
+    dominant = "gate_up" if gu_ms >= dn_ms else "down"
+    dom_bytes, dom_ms = (gateup_bytes, gu_ms) if dominant == "gate_up" else (down_bytes, dn_ms)
+    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
+    roofline = {"kernel": f"grouped_gemm_kernel<{2 if dominant == 'gate_up' else 1}> ({dominant})",
+                "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_source": peak_src, "traffic": None,
+                "algorithmic_bytes_per_launch": dom_bytes}
+    layer_bytes = gateup_bytes + down_bytes
+    layer_ms = sum(stage_ms)
+
+    # ------------------------------------------------------------------ e2e
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    x_in = torch.empty_like(x)
+    for _ in range(3):
+        x_in.copy_(x_host, non_blocking=True)
+        out_host.copy_(step(x_in), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        x_in.copy_(x_host, non_blocking=True)
+        out_host.copy_(step(x_in), non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e2.elapsed_time(e3) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * T / (float(e2e_ms.item()) / 1000.0)
+    status = Workspace.get(dev).status()
+
+    # ---------------------------------------------------------- CPU oracle
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        def get_expert(e):
+            return {p: (w.cpu(), s.cpu()) for p, (w, s) in bank.views(e + 1).items()}
+
+        cache = {}
+
+        def cached(e):
+            if e not in cache:
+                cache[e] = get_expert(e)
+            return cache[e]
+
+        shared = {p: (w.cpu(), s.cpu()) for p, (w, s) in bank.views(0).items()}
+        v, n, dt = cpu_sample(x.cpu(), store.get_gate_weight(LAYER).cpu(), cached, shared, args.cpu_budget_s, 64)
+        cpu = {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{n} tokens of the T={T} batch through the oracle's per-token restatement of the "
+                         f"reference moe_block in {dt:.1f} s; tokens/s extrapolates linearly in T"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) FP8 block-quantised experts)",
+            "config": {"workload": f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, 256+1 experts "
+                                   f"resident (config 2)" + ("; replicas per rank" if world > 1 else ""),
+                       "tokens_per_gpu": T, "hidden": H, "moe_intermediate": F, "experts": E, "top_k": TOPK,
+                       "router": "ref", "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
+                       "parallelism": f"replica x{world}" if world > 1 else "single GPU"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2},
+            "roofline": roofline,
+            "stages_ms": {"router": stage_ms[0], "permute": stage_ms[1], "gate_up": gu_ms, "down": dn_ms,
+                          "combine": stage_ms[4]},
+            "layer": {"algorithmic_bytes": layer_bytes, "GB_s": layer_bytes / (layer_ms / 1e3) / 1e9,
+                      "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm_peak,
+                      "fp8_tflops_algorithmic": algo_flops / (ms_max / 1e3) / 1e12,
+                      "fp8_frac_of_nominal_dense": algo_flops / (ms_max / 1e3) / 1e12 / FP8_DENSE_NOMINAL_TFLOPS,
+                      "experts_touched": touched},
+            "gpu_launches": 8 * args.steps,
+            "device_status": status,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

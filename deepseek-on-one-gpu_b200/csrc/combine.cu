@@ -1,0 +1,65 @@
+// K5: weighted combine / un-permute with the shared expert.
+//
+// For token t, with y the down-projection rows (bf16, one per (token, k)
+// pair and one shared-expert row per token):
+//   acc = 0 (bf16)
+//   for k in 0..top_k-1:  acc = bf16(acc + bf16(bf16(w[t,k]) * y[pos[t,k]]))
+//   out[t] = bf16(y_shared[t] + bf16(acc * scale))
+// This is the reference's arithmetic (inference/forward.py:137,151,153): the
+// fp32 0-dim weight times a bf16 row yields bf16 (the weight is rounded to
+// bf16 by type promotion), the running sum is bf16 and accumulates in top-k
+// order, and the final ``shared + routed * routed_scaling_factor`` is bf16.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsmoe {
+
+namespace cb {
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ y, int T, int H,
+                                                      const int32_t* __restrict__ pos,
+                                                      const float* __restrict__ w, int top_k,
+                                                      const int32_t* __restrict__ row_start, float scale,
+                                                      __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  __shared__ int s_row[8];
+  __shared__ float s_w[8];
+  if (threadIdx.x < top_k) {
+    s_row[threadIdx.x] = pos[static_cast<size_t>(t) * top_k + threadIdx.x];
+    s_w[threadIdx.x] = bf16_round(w[static_cast<size_t>(t) * top_k + threadIdx.x]);
+  }
+  __syncthreads();
+  const int srow = row_start[0] + t;
+  const int nchunks = H / 8;
+  for (int c = threadIdx.x; c < nchunks; c += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int k = 0; k < top_k; ++k) {
+      const int r = s_row[k];
+      if (r < 0) continue;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(r) * H) + c);
+      const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
+      const float wk = s_w[k];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = bf16_round(acc[i] + bf16_round(wk * __bfloat162float(vb[i])));
+    }
+    const uint4 sv = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(srow) * H) + c);
+    const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(&sv);
+    uint4 o;
+    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      ob[i] = __float2bfloat16_rn(__bfloat162float(sb[i]) + bf16_round(acc[i] * scale));
+    reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H)[c] = o;
+  }
+}
+}  // namespace cb
+
+cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
+                           const int32_t* row_start, float scale, __nv_bfloat16* out, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  cb::combine_kernel<<<T, 256, 0, stream>>>(y, T, H, pos, w, top_k, row_start, scale, out);
+  return cudaGetLastError();
+}
+
+}  // namespace dsmoe

@@ -1,0 +1,55 @@
+// Internal launch interface between the C ABI (api.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsmoe {
+
+// Group-table convention used by every kernel: group 0 is the shared expert
+// (every token, in token order), group 1 + e is routed expert e.
+struct GemmParams {
+  const int32_t* counts;      // [n_groups] tokens per group
+  const int32_t* row_start;   // [n_groups] first permuted row (multiple of 32)
+  const int32_t* unit_start;  // [n_groups + 1] prefix sum of work units
+  const int32_t* slot_of;     // [n_groups] weight-bank slot of each group
+  const float* wscale0;       // [n_slots][M/128][K/128]
+  const float* wscale1;       // second weight (gate/up only)
+  int n_groups;
+  int n_slots;
+  int M;  // weight rows per expert (output features)
+  int K;  // reduction length
+  int P;  // rows of one activation half (hi rows [0,P), lo rows [P,2P))
+  uint8_t* hq;          // gate/up output: e4m3 [2P][M]
+  float* hs;            // gate/up output scales: [M/128][P]
+  __nv_bfloat16* y;     // down output: bf16 [P][M]
+  int* status;          // device error word
+};
+
+int gemm_smem_bytes(int nb);
+cudaError_t launch_grouped_gemm(int nb, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
+                                const CUtensorMap& sx, const GemmParams& p, int grid, cudaStream_t stream);
+
+// Router (router.cu)
+int router_ksplit(int T, int H, int E, int num_sms);
+cudaError_t launch_router_logits(const void* x, const void* gate, float* partial, int T, int H, int E, int ksplit,
+                                 cudaStream_t stream);
+cudaError_t launch_router_select(const float* partial, int ksplit, const float* bias, int T, int E, int n_group,
+                                 int topk_group, int top_k, int mode, int norm, float scaling, int32_t* idx,
+                                 int64_t* idx64, float* w, cudaStream_t stream);
+
+// Permutation (permute.cu)
+cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream);
+cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int mt_up, int mt_dn, int32_t* row_start,
+                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, int32_t* bad, cudaStream_t stream);
+cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int has_shared,
+                                 const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq, float* sx,
+                                 int32_t* pos, cudaStream_t stream);
+
+// Combine (combine.cu)
+cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
+                           const int32_t* row_start, float scale, __nv_bfloat16* out, cudaStream_t stream);
+
+}  // namespace dsmoe

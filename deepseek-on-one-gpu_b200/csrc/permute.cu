@@ -1,0 +1,189 @@
+// K2: token permutation by expert, fused with the FP8 hi/lo activation split.
+//
+// The reference loops over tokens and runs each token's 8 experts one at a
+// time (inference/forward.py:140-151). Here tokens are grouped by expert so
+// that each expert's weights are read once for all of its tokens:
+//   count   histogram of (token, k) pairs per expert group
+//   plan    exclusive scans -> 32-row-aligned segment starts, work-unit starts
+//           of both GEMMs (one block)
+//   scatter one warp per token: claims one row in each of its experts'
+//           segments (+ its row in the shared-expert segment), splits the bf16
+//           row into hi/lo e4m3 terms with one fp32 scale per 128 columns,
+//           writes the row copies and records the (token, k) -> row map used
+//           by the combine.
+// Activation format (per row r, 128-column block b):
+//   sx = amax / 448;  q = x * 448 / amax;  hi = e4m3(q);  lo = e4m3(q - hi)
+//   x ~= (hi + lo) * sx   (about 8 significant bits instead of 4).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsmoe {
+
+namespace pm {
+constexpr int MAX_GROUPS = 512;
+
+__global__ void __launch_bounds__(256) count_kernel(const int32_t* __restrict__ idx, int n_pairs,
+                                                    int32_t* __restrict__ counts, int n_groups) {
+  __shared__ int hist[MAX_GROUPS];
+  for (int i = threadIdx.x; i < n_groups; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n_pairs; p += gridDim.x * blockDim.x) {
+    const int g = idx[p] + 1;
+    if (g >= 1 && g < n_groups) atomicAdd(&hist[g], 1);
+  }
+  __syncthreads();
+  for (int i = 1 + threadIdx.x; i < n_groups; i += blockDim.x)
+    if (hist[i]) atomicAdd(&counts[i], hist[i]);
+}
+
+template <int N>
+__device__ __forceinline__ int block_excl_scan(int v, int* buf) {
+  // Hillis-Steele inclusive scan over blockDim.x == N entries, then shift.
+  const int i = threadIdx.x;
+  buf[i] = v;
+  __syncthreads();
+  for (int o = 1; o < N; o <<= 1) {
+    const int add = i >= o ? buf[i - o] : 0;
+    __syncthreads();
+    buf[i] += add;
+    __syncthreads();
+  }
+  const int incl = buf[i];
+  __syncthreads();
+  return incl - v;
+}
+
+__global__ void __launch_bounds__(MAX_GROUPS) plan_kernel(int32_t* __restrict__ counts, int n_groups,
+                                                          int shared_tokens, int mt_up, int mt_dn,
+                                                          int32_t* __restrict__ row_start,
+                                                          int32_t* __restrict__ cursor,
+                                                          int32_t* __restrict__ ustart_up,
+                                                          int32_t* __restrict__ ustart_dn) {
+  __shared__ int buf[MAX_GROUPS];
+  const int i = threadIdx.x;
+  int c = 0;
+  if (i < n_groups) c = i == 0 ? shared_tokens : counts[i];
+  __syncthreads();
+  if (i == 0) counts[0] = shared_tokens;
+  const int nt = (c + 127) / 128;
+  const int seg = block_excl_scan<MAX_GROUPS>((c + 31) & ~31, buf);
+  const int uu = block_excl_scan<MAX_GROUPS>(mt_up * nt, buf);
+  const int ud = block_excl_scan<MAX_GROUPS>(mt_dn * nt, buf);
+  if (i <= n_groups) {
+    row_start[i] = seg;
+    if (ustart_up) ustart_up[i] = uu;
+    if (ustart_dn) ustart_dn[i] = ud;
+  }
+  if (i < n_groups) cursor[i] = 0;
+}
+
+__global__ void __launch_bounds__(256) quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                            const int32_t* __restrict__ idx, int top_k,
+                                                            int has_shared, const int32_t* __restrict__ row_start,
+                                                            int32_t* __restrict__ cursor, int P,
+                                                            uint8_t* __restrict__ xq, float* __restrict__ sx,
+                                                            int32_t* __restrict__ pos) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  int myrow = -1;
+  if (lane < top_k) {
+    const int g = idx[static_cast<size_t>(t) * top_k + lane] + 1;
+    myrow = row_start[g] + atomicAdd(&cursor[g], 1);
+    pos[static_cast<size_t>(t) * top_k + lane] = myrow;
+  }
+  int rows[9];
+  int n = 0;
+  if (has_shared) rows[n++] = row_start[0] + t;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = __shfl_sync(0xffffffffu, myrow, k);
+    if (k < top_k) rows[has_shared + k] = r;
+  }
+  n += top_k;
+  const int nblk = H / 128;
+  const int iters = (nblk + 1) / 2;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(t) * H;
+  uint8_t* xq_lo = xq + static_cast<size_t>(P) * H;
+  for (int it = 0; it < iters; ++it) {
+    const int blk = it * 2 + (lane >> 4);
+    const bool active = blk < nblk;
+    const int col = blk * 128 + (lane & 15) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (active) v = __ldg(reinterpret_cast<const uint4*>(xr + col));
+    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
+    float f[8];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      f[i] = __bfloat162float(vb[i]);
+      amax = fmaxf(amax, fabsf(f[i]));
+    }
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 448.f / amax : 0.f;
+    const float scale = amax / 448.f;
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const float q0 = f[i] * inv, q1 = f[i + 1] * inv;
+      const uint16_t h2 = f32x2_to_e4m3x2(q0, q1);
+      const float h0 = e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff));
+      const float h1 = e4m3_to_f32(static_cast<uint8_t>(h2 >> 8));
+      const uint16_t l2 = f32x2_to_e4m3x2(q0 - h0, q1 - h1);
+      const int w = i >> 2, sh = (i & 2) * 8;
+      if (sh == 0) {
+        hw[w] = h2;
+        lw[w] = l2;
+      } else {
+        hw[w] |= static_cast<uint32_t>(h2) << 16;
+        lw[w] |= static_cast<uint32_t>(l2) << 16;
+      }
+    }
+    if (active) {
+      const uint2 hv = make_uint2(hw[0], hw[1]);
+      const uint2 lv = make_uint2(lw[0], lw[1]);
+#pragma unroll
+      for (int r = 0; r < 9; ++r) {
+        if (r < n) {
+          const size_t off = static_cast<size_t>(rows[r]) * H + col;
+          *reinterpret_cast<uint2*>(xq + off) = hv;
+          *reinterpret_cast<uint2*>(xq_lo + off) = lv;
+          if ((lane & 15) == 0) sx[static_cast<size_t>(blk) * P + rows[r]] = scale;
+        }
+      }
+    }
+  }
+}
+}  // namespace pm
+
+cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream) {
+  if (n_groups > pm::MAX_GROUPS) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * n_groups, stream);
+  if (e != cudaSuccess) return e;
+  if (n_pairs == 0) return cudaSuccess;
+  int blocks = (n_pairs + 255) / 256;
+  if (blocks > 296) blocks = 296;
+  pm::count_kernel<<<blocks, 256, 0, stream>>>(idx, n_pairs, counts, n_groups);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int mt_up, int mt_dn, int32_t* row_start,
+                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, int32_t*, cudaStream_t stream) {
+  if (n_groups + 1 > pm::MAX_GROUPS) return cudaErrorInvalidValue;
+  pm::plan_kernel<<<1, pm::MAX_GROUPS, 0, stream>>>(counts, n_groups, shared_tokens, mt_up, mt_dn, row_start, cursor,
+                                                    ustart_up, ustart_dn);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int has_shared,
+                                 const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq, float* sx,
+                                 int32_t* pos, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int blocks = (T * 32 + 255) / 256;
+  pm::quant_scatter_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, idx, top_k,
+                                                       has_shared, row_start, cursor, P, xq, sx, pos);
+  return cudaGetLastError();
+}
+
+}  // namespace dsmoe

@@ -1,0 +1,157 @@
+"""ctypes binding of ``libdsmoe.so`` (the C ABI in ``include/dsmoe.h``).
+
+There is no fallback: if the library is missing or a call fails, a
+``RuntimeError`` is raised. Workspaces are cached per device and grown on
+demand; the library itself never allocates.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdsmoe.so")
+
+ROUTER_MODES = {"ref": 0, "v3": 1}
+ERRORS = {-1: "invalid argument", -2: "CUDA error", -3: "workspace too small", -4: "unsupported", -5: "device error"}
+
+EXPORTED = (
+    "dsmoe_last_error", "dsmoe_version", "dsmoe_workspace_size", "dsmoe_route", "dsmoe_moe_forward",
+    "dsmoe_moe_experts", "dsmoe_expert_ffn_workspace_size", "dsmoe_fp8_linear_workspace_size",
+    "dsmoe_expert_ffn", "dsmoe_fp8_linear", "dsmoe_read_status", "dsmoe_set_profile_events",
+)
+
+
+class MoeConfig(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int32), ("inter", ctypes.c_int32), ("n_routed", ctypes.c_int32),
+        ("n_group", ctypes.c_int32), ("topk_group", ctypes.c_int32), ("top_k", ctypes.c_int32),
+        ("router_mode", ctypes.c_int32), ("norm_topk_prob", ctypes.c_int32),
+        ("routed_scaling_factor", ctypes.c_float),
+    ]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [
+        ("gate_weight", ctypes.c_void_p), ("score_bias", ctypes.c_void_p), ("n_slots", ctypes.c_int32),
+        ("w_gate", ctypes.c_void_p), ("s_gate", ctypes.c_void_p),
+        ("w_up", ctypes.c_void_p), ("s_up", ctypes.c_void_p),
+        ("w_down", ctypes.c_void_p), ("s_down", ctypes.c_void_p),
+        ("slot_of_expert", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(f"libdsmoe.so is not built ({LIB_PATH}); run __graft_entry__.build()")
+                L = ctypes.CDLL(LIB_PATH)
+                vp, i32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
+                cfgp = ctypes.POINTER(MoeConfig)
+                wp = ctypes.POINTER(LayerWeights)
+                L.dsmoe_last_error.restype = ctypes.c_char_p
+                L.dsmoe_version.restype = ctypes.c_int
+                L.dsmoe_workspace_size.argtypes = [cfgp, i32]
+                L.dsmoe_workspace_size.restype = sz
+                L.dsmoe_route.argtypes = [cfgp, vp, vp, vp, i32, vp, vp, vp, sz, vp]
+                L.dsmoe_moe_forward.argtypes = [cfgp, wp, vp, i32, vp, vp, vp, vp, sz, vp]
+                L.dsmoe_moe_experts.argtypes = [cfgp, wp, vp, i32, vp, vp, sz, vp]
+                L.dsmoe_expert_ffn_workspace_size.argtypes = [i32, i32, i32]
+                L.dsmoe_expert_ffn_workspace_size.restype = sz
+                L.dsmoe_fp8_linear_workspace_size.argtypes = [i32, i32, i32]
+                L.dsmoe_fp8_linear_workspace_size.restype = sz
+                L.dsmoe_expert_ffn.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
+                L.dsmoe_fp8_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, sz, vp]
+                L.dsmoe_read_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
+                L.dsmoe_set_profile_events.argtypes = [ctypes.POINTER(vp), i32]
+                for name in EXPORTED:
+                    getattr(L, name).restype = getattr(L, name).restype or ctypes.c_int
+                _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().dsmoe_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({ERRORS.get(rc, rc)}): {msg}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("dsmoe runs on CUDA tensors only (no CPU fallback)")
+        if not t.is_contiguous():
+            raise RuntimeError("dsmoe expects contiguous tensors")
+
+
+class Workspace:
+    """Per-device scratch buffer, zero-initialised once (the first bytes hold
+    the device error word) and grown on demand."""
+
+    _by_device: dict[int, "Workspace"] = {}
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.buf = torch.zeros(0, dtype=torch.uint8, device=device)
+
+    @classmethod
+    def get(cls, device: torch.device) -> "Workspace":
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        ws = cls._by_device.get(idx)
+        if ws is None:
+            ws = cls._by_device[idx] = Workspace(torch.device("cuda", idx))
+        return ws
+
+    def ensure(self, nbytes: int) -> torch.Tensor:
+        if self.buf.numel() < nbytes:
+            # Grow by 25 % to avoid re-allocating for every new token count.
+            self.buf = torch.zeros(int(nbytes * 1.25) + 4096, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+    def status(self) -> int:
+        st = ctypes.c_int32(0)
+        lib().dsmoe_read_status(ptr(self.buf), ctypes.byref(st), stream_handle(self.device))
+        return int(st.value)
+
+
+def moe_config(config) -> MoeConfig:
+    mode = getattr(config, "router_mode", "ref")
+    return MoeConfig(
+        hidden=config.hidden_size, inter=config.moe_intermediate_size, n_routed=config.n_routed_experts,
+        n_group=config.n_group, topk_group=config.topk_group, top_k=config.num_experts_per_tok,
+        router_mode=ROUTER_MODES[mode], norm_topk_prob=int(bool(config.norm_topk_prob)),
+        routed_scaling_factor=float(config.routed_scaling_factor),
+    )
+
+
+def set_profile_events(events: list | None) -> None:
+    """Record ``events`` (torch.cuda.Event, up to 8) at the stage boundaries of
+    later MoE calls from this thread; ``None`` switches it off."""
+    if not events:
+        check(lib().dsmoe_set_profile_events(None, 0), "dsmoe_set_profile_events")
+        return
+    for e in events:
+        if e.cuda_event == 0:  # torch creates the CUDA event lazily
+            e.record()
+    arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+    check(lib().dsmoe_set_profile_events(arr, len(events)), "dsmoe_set_profile_events")

@@ -1,0 +1,77 @@
+"""Drop-in ``moe_block`` (``inference/forward.py:112-153``).
+
+Same signature and result as the reference: ``hidden`` [B, S, H] bf16 ->
+``shared_expert(hidden) + routed_scaling_factor * sum_k w_k expert_k(hidden)``
+in bf16. The reference routes, then loops over tokens copying each token's 8
+experts to the GPU and running 8 single-token FFNs; here the whole block is
+one sequence of CUDA kernels on the current stream:
+
+  router -> permute + FP8 hi/lo split -> grouped gate/up GEMM (+SiLU*mul)
+  -> grouped down GEMM -> weighted combine with the shared expert.
+
+``gpu_transfer`` must be this package's ``GPUTransfer``: it owns the layer's
+device weight bank. In streaming mode (fewer slots than experts) the routing is
+read back once per block (the reference reads it back once per token, via
+``.tolist()``) to bring missing experts in before the expert GEMMs.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr, require_cuda, stream_handle
+
+
+def _layer_weights(bank, gate_weight, bias) -> _lib.LayerWeights:
+    return _lib.LayerWeights(
+        gate_weight=ptr(gate_weight), score_bias=ptr(bias), n_slots=bank.n_slots,
+        w_gate=ptr(bank.w["gate_proj"]), s_gate=ptr(bank.s["gate_proj"]),
+        w_up=ptr(bank.w["up_proj"]), s_up=ptr(bank.s["up_proj"]),
+        w_down=ptr(bank.w["down_proj"]), s_down=ptr(bank.s["down_proj"]),
+        slot_of_expert=ptr(bank.slot_of),
+    )
+
+
+def moe_block(hidden: torch.Tensor, layer_idx: int, weight_store, gpu_transfer, config,
+              verbose: bool = False, return_routing: bool = False):
+    if not hasattr(gpu_transfer, "ensure_resident"):
+        raise TypeError("moe_block needs dsmoe.GPUTransfer (it owns the device expert bank)")
+    H = hidden.shape[-1]
+    x = hidden.reshape(-1, H)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("moe_block expects bf16 hidden states")
+    x = x.contiguous()
+    T = x.shape[0]
+    gate_weight = weight_store.get_gate_weight(layer_idx)
+    bias = None
+    if getattr(config, "router_mode", "ref") == "v3":
+        bias = weight_store.get_gate_bias(layer_idx)
+    require_cuda(x, gate_weight, bias)
+    cfg = _lib.moe_config(config)
+    K = cfg.top_k
+    out = torch.empty_like(x)
+    idx = torch.empty(T, K, dtype=torch.int64, device=x.device)
+    w = torch.empty(T, K, dtype=torch.float32, device=x.device)
+    ws = _lib.Workspace.get(x.device).ensure(lib().dsmoe_workspace_size(cfg, T))
+    stream = stream_handle(x.device)
+    bank = gpu_transfer.bank(layer_idx)
+    if bank.fully_resident:
+        lw = _layer_weights(bank, gate_weight, bias)
+        check(lib().dsmoe_moe_forward(cfg, lw, ptr(x), T, ptr(out), ptr(idx), ptr(w), ptr(ws), ws.numel(), stream),
+              "dsmoe_moe_forward")
+    else:
+        check(lib().dsmoe_route(cfg, ptr(x), ptr(gate_weight), ptr(bias), T, ptr(idx), ptr(w), ptr(ws), ws.numel(),
+                                stream), "dsmoe_route")
+        experts = torch.unique(idx).tolist()  # one device->host read per block
+        if verbose:
+            print(f"      [moe L{layer_idx:02d}] {T} tokens -> {len(experts)} distinct experts")
+        bank = gpu_transfer.ensure_resident(layer_idx, experts)
+        lw = _layer_weights(bank, gate_weight, bias)
+        check(lib().dsmoe_moe_experts(cfg, lw, ptr(x), T, ptr(out), ptr(ws), ws.numel(), stream),
+              "dsmoe_moe_experts")
+    gpu_transfer.mark_used(layer_idx)
+    out = out.view(hidden.shape)
+    if return_routing:
+        shape = tuple(hidden.shape[:-1]) + (K,)
+        return out, idx.view(shape), w.view(shape)
+    return out

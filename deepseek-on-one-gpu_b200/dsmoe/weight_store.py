@@ -1,0 +1,130 @@
+"""Host-side expert storage: the pinned-RAM LRU and a synthetic weight store.
+
+``ExpertCache`` keeps the reference's interface and policy
+(``inference/weight_store.py:42-78``): entries keyed ``(layer, expert)`` hold
+``{proj: {"weight", "weight_scale_inv"}}`` pinned tensors; ``get`` refreshes
+recency, ``put`` evicts least-recently-used entries until the new entry fits
+the byte capacity. Hit/miss counters are added.
+
+``SyntheticWeightStore`` answers the calls the MoE path makes on the
+reference's ``WeightStore`` (``get_gate_weight`` :252, ``get_shared_expert_weights``
+:244, ``get_expert`` :185) with seeded synthetic FP8 weights, so the block can
+run without the 689 GB checkpoint. It also adds ``get_gate_bias`` (the
+``e_score_correction_bias`` the bias-corrected router needs) and
+``fill_bank``, which generates a whole layer directly on the GPU.
+"""
+from __future__ import annotations
+
+from collections import OrderedDict
+
+import torch
+
+from .synthetic import PROJS, SHARED, SyntheticLayer, expert_weights
+
+
+class ExpertCache:
+    def __init__(self, capacity_bytes: int):
+        self.capacity = int(capacity_bytes)
+        self.used = 0
+        self.entries: OrderedDict[tuple[int, int], dict] = OrderedDict()
+        self.hits = 0
+        self.misses = 0
+
+    @staticmethod
+    def entry_bytes(expert_dict: dict) -> int:
+        return sum(t.nbytes for proj in expert_dict.values() for t in proj.values())
+
+    def get(self, layer: int, expert_idx: int) -> dict | None:
+        key = (layer, expert_idx)
+        entry = self.entries.get(key)
+        if entry is None:
+            self.misses += 1
+            return None
+        self.hits += 1
+        self.entries.move_to_end(key)
+        return entry
+
+    def put(self, layer: int, expert_idx: int, expert_dict: dict) -> None:
+        need = self.entry_bytes(expert_dict)
+        self._evict_until(need)
+        self.entries[(layer, expert_idx)] = expert_dict
+        self.used += need
+
+    def _evict_until(self, needed: int) -> None:
+        while self.entries and self.used + needed > self.capacity:
+            _, old = self.entries.popitem(last=False)
+            self.used -= self.entry_bytes(old)
+
+
+class SyntheticWeightStore:
+    """Seeded stand-in for the reference's ``WeightStore`` on the MoE path."""
+
+    def __init__(self, config, seed: int, device, expert_cache_bytes: int = 16 * 1024 ** 3,
+                 pin_memory: bool = True, bias_zipf: float | None = None, layer_seeds: dict | None = None,
+                 gen_device: str = "cpu"):
+        self.config = config
+        self.gen_device = gen_device
+        self.seed = seed
+        self.device = torch.device(device)
+        self.pin_memory = pin_memory and torch.cuda.is_available()
+        self.bias_zipf = bias_zipf
+        self.layer_seeds = layer_seeds or {}
+        self.expert_cache = ExpertCache(expert_cache_bytes)
+        self._layers: dict[int, SyntheticLayer] = {}
+        self._gate: dict[int, torch.Tensor] = {}
+        self._bias: dict[int, torch.Tensor] = {}
+        self._shared: dict[int, dict] = {}
+
+    def _seed(self, layer: int) -> int:
+        return self.layer_seeds.get(layer, self.seed)
+
+    def layer(self, layer: int) -> SyntheticLayer:
+        if layer not in self._layers:
+            c = self.config
+            self._layers[layer] = SyntheticLayer(self._seed(layer), layer, c.hidden_size, c.moe_intermediate_size,
+                                                 c.n_routed_experts, "cpu", bias_zipf=self.bias_zipf, cache=False)
+        return self._layers[layer]
+
+    def get_gate_weight(self, layer: int) -> torch.Tensor:
+        if layer not in self._gate:
+            self._gate[layer] = self.layer(layer).gate.to(self.device)
+        return self._gate[layer]
+
+    def get_gate_bias(self, layer: int) -> torch.Tensor:
+        if layer not in self._bias:
+            self._bias[layer] = self.layer(layer).bias.to(self.device)
+        return self._bias[layer]
+
+    def get_shared_expert_weights(self, layer: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+        if layer not in self._shared:
+            ew = self.layer(layer).shared()
+            self._shared[layer] = {p: (w.to(self.device), s.to(self.device)) for p, (w, s) in ew.items()}
+        return self._shared[layer]
+
+    def get_expert(self, layer: int, expert_idx: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+        cached = self.expert_cache.get(layer, expert_idx)
+        if cached is None:
+            ew = self.layer(layer).expert(expert_idx)
+            cached = {}
+            for p, (w, s) in ew.items():
+                if self.pin_memory:
+                    w, s = w.pin_memory(), s.pin_memory()
+                cached[p] = {"weight": w, "weight_scale_inv": s}
+            self.expert_cache.put(layer, expert_idx, cached)
+        return {p: (cached[p]["weight"], cached[p]["weight_scale_inv"]) for p in PROJS}
+
+    def fill_bank(self, layer: int, bank, experts=None) -> None:
+        """Write the shared expert and `experts` (default: all) into a device
+        ``LayerBank``. With ``gen_device="cuda"`` they are generated on the GPU
+        by the CUDA generator (fast, but different values from the CPU
+        generator that the oracle uses); with ``"cpu"`` they are the same bytes
+        ``layer(l).expert(e)`` returns."""
+        c = self.config
+        experts = range(c.n_routed_experts) if experts is None else experts
+        for e in [SHARED, *experts]:
+            if self.gen_device == "cpu":
+                ew = self.layer(layer).expert(e)
+            else:
+                ew = expert_weights(self._seed(layer), layer, e, c.hidden_size, c.moe_intermediate_size,
+                                    device=bank.device)
+            bank.write_slot(bank.assign(0 if e == SHARED else e + 1), ew)

@@ -1,0 +1,160 @@
+/*
+ * libdsmoe — B200-native (sm_100a) DeepSeek-R1 MoE block, C ABI.
+ *
+ * Drop-in boundary for the MoE hot path of sushruta/deepseek-on-one-gpu.
+ * Every entry point below replaces one Python function of the reference
+ * (cited as path:line inside that project). Arguments are raw device
+ * pointers, sizes and a cudaStream_t; no framework types cross the ABI.
+ *
+ * Conventions
+ *   - Every function returns 0 (DSMOE_OK) or a negative DSMOE_ERR_* code and
+ *     never throws; dsmoe_last_error() returns a message for the calling
+ *     thread's last failure.
+ *   - All work is enqueued on `stream`; nothing blocks the host, nothing is
+ *     allocated. Scratch memory comes from the caller ("workspace"), sized by
+ *     the matching *_workspace_size() function.
+ *   - Tensors are dense row-major: bf16 activations [tokens, hidden]; e4m3
+ *     weights [out, in] with fp32 weight_scale_inv [out/128, in/128] that
+ *     multiplies on dequantisation (the checkpoint format).
+ *   - Expert groups: group 0 is the shared expert, group 1 + e is routed
+ *     expert e. A weight bank holds n_slots experts; slot_of_expert maps each
+ *     group to its slot.
+ *   - Device errors (a bounded wait that timed out inside a kernel, a bad
+ *     slot) are recorded in the workspace; dsmoe_read_status() fetches them.
+ */
+#ifndef DSMOE_H
+#define DSMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSMOE_API __attribute__((visibility("default")))
+#else
+#define DSMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* dsmoe_stream_t; /* == cudaStream_t */
+
+enum {
+  DSMOE_OK = 0,
+  DSMOE_ERR_INVALID = -1,     /* bad argument (shape, pointer, alignment) */
+  DSMOE_ERR_CUDA = -2,        /* a CUDA runtime/driver call failed */
+  DSMOE_ERR_WORKSPACE = -3,   /* workspace too small */
+  DSMOE_ERR_UNSUPPORTED = -4, /* shape or mode this build does not handle */
+  DSMOE_ERR_DEVICE = -5       /* a kernel reported an error (see dsmoe_read_status) */
+};
+
+enum { DSMOE_ROUTER_REF = 0, DSMOE_ROUTER_V3 = 1 };
+
+/* MoE fields of DeepSeekConfig (inference/config.py:32-52). */
+typedef struct {
+  int32_t hidden;          /* hidden_size, multiple of 128 */
+  int32_t inter;           /* moe_intermediate_size, multiple of 128 */
+  int32_t n_routed;        /* n_routed_experts = 32 * n_group */
+  int32_t n_group;         /* <= 8 */
+  int32_t topk_group;
+  int32_t top_k;           /* num_experts_per_tok, <= 8 */
+  int32_t router_mode;     /* DSMOE_ROUTER_REF or DSMOE_ROUTER_V3 */
+  int32_t norm_topk_prob;
+  float routed_scaling_factor;
+} dsmoe_moe_config_t;
+
+/* Device-resident expert weights of one MoE layer. */
+typedef struct {
+  const void* gate_weight;        /* bf16 [n_routed, hidden] */
+  const float* score_bias;        /* fp32 [n_routed] (router v3) or NULL */
+  int32_t n_slots;                /* experts held by the bank */
+  const void* w_gate;             /* e4m3 [n_slots, inter, hidden] */
+  const float* s_gate;            /* fp32 [n_slots, inter/128, hidden/128] */
+  const void* w_up;               /* e4m3 [n_slots, inter, hidden] */
+  const float* s_up;              /* fp32 [n_slots, inter/128, hidden/128] */
+  const void* w_down;             /* e4m3 [n_slots, hidden, inter] */
+  const float* s_down;            /* fp32 [n_slots, hidden/128, inter/128] */
+  const int32_t* slot_of_expert;  /* device int32 [n_routed + 1]: group -> slot */
+} dsmoe_layer_weights_t;
+
+DSMOE_API const char* dsmoe_last_error(void);
+DSMOE_API int dsmoe_version(void);
+
+/* Scratch bytes for dsmoe_route / dsmoe_moe_forward / dsmoe_moe_experts at `tokens`. */
+DSMOE_API size_t dsmoe_workspace_size(const dsmoe_moe_config_t* cfg, int32_t tokens);
+
+/*
+ * Router. Replaces route() (inference/ops.py:209-257) for router_mode REF;
+ * REF ignores `score_bias` and applies no scaling factor (the reference
+ * scales after the combine, inference/forward.py:153). V3 selects on
+ * sigmoid + bias with top-2-sum group scores and returns weights already
+ * multiplied by routed_scaling_factor.
+ *   hidden [tokens, hidden] bf16 -> topk_idx [tokens, top_k] int64 (descending
+ *   score), topk_w [tokens, top_k] fp32.
+ */
+DSMOE_API int dsmoe_route(const dsmoe_moe_config_t* cfg, const void* hidden, const void* gate_weight,
+                const float* score_bias, int32_t tokens, int64_t* topk_idx, float* topk_w, void* workspace,
+                size_t workspace_bytes, dsmoe_stream_t stream);
+
+/*
+ * Full MoE block. Replaces moe_block() (inference/forward.py:112-153):
+ * route -> permute -> grouped FP8 gate/up (+SiLU*mul) -> grouped FP8 down ->
+ * weighted combine with the shared expert. Every routed expert the routing
+ * selects and the shared expert must be resident in `w` (slot_of_expert).
+ *   hidden [tokens, hidden] bf16 -> out [tokens, hidden] bf16.
+ * topk_idx / topk_w (optional, may be NULL) receive the routing as dsmoe_route.
+ */
+DSMOE_API int dsmoe_moe_forward(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden,
+                      int32_t tokens, void* out, int64_t* topk_idx, float* topk_w, void* workspace,
+                      size_t workspace_bytes, dsmoe_stream_t stream);
+
+/*
+ * Second half of dsmoe_moe_forward, for callers that route first and make the
+ * selected experts resident afterwards (the expert-streaming path of
+ * GPUTransfer.transfer_experts, inference/gpu_transfer.py:50-89): consumes the
+ * routing that the preceding dsmoe_route left in the same workspace.
+ */
+DSMOE_API int dsmoe_moe_experts(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden,
+                      int32_t tokens, void* out, void* workspace, size_t workspace_bytes, dsmoe_stream_t stream);
+
+/* Scratch bytes for dsmoe_expert_ffn / dsmoe_fp8_linear. */
+DSMOE_API size_t dsmoe_expert_ffn_workspace_size(int32_t tokens, int32_t hidden, int32_t inter);
+DSMOE_API size_t dsmoe_fp8_linear_workspace_size(int32_t tokens, int32_t in_features, int32_t out_features);
+
+/*
+ * One expert FFN. Replaces expert_ffn() / swiglu() (inference/ops.py:186-206):
+ * down(silu(gate(x)) * up(x)).   x [tokens, hidden] bf16 -> out [tokens, hidden] bf16.
+ */
+DSMOE_API int dsmoe_expert_ffn(const void* x, int32_t tokens, int32_t hidden, int32_t inter, const void* w_gate,
+                     const float* s_gate, const void* w_up, const float* s_up, const void* w_down,
+                     const float* s_down, void* out, void* workspace, size_t workspace_bytes,
+                     dsmoe_stream_t stream);
+
+/*
+ * FP8 block-quantised linear. Replaces fp8_linear() (inference/ops.py:15-44)
+ * for in/out features that are multiples of 128:
+ *   out[t, o] = bf16( sum_i x[t, i] * weight[o, i] * scale_inv[o/128, i/128] ).
+ */
+DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_features, int32_t out_features,
+                     const void* weight, const float* scale_inv, void* out, void* workspace,
+                     size_t workspace_bytes, dsmoe_stream_t stream);
+
+/*
+ * Measurement hook (no reference counterpart; the reference has no profiler
+ * hooks). Registers up to 8 cudaEvent_t handles that the calling thread's
+ * later dsmoe_moe_forward / dsmoe_moe_experts calls record on their stream at
+ * stage boundaries: [0] before the router, [1] after it, [2] after the
+ * permute, [3] after the gate/up GEMM, [4] after the down GEMM, [5] after the
+ * combine. n = 0 switches it off.
+ */
+DSMOE_API int dsmoe_set_profile_events(void* const* events, int32_t n);
+
+/* Reads (synchronously) and clears the device error word kept in `workspace`. */
+DSMOE_API int dsmoe_read_status(void* workspace, int32_t* device_status, dsmoe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSMOE_H */

@@ -1,0 +1,85 @@
+"""The CPU oracle is pinned to the reference: golden vectors in tests/golden
+are outputs of the reference's own route() and moe_block() (made by
+tests/golden/make_golden.py)."""
+import os
+
+import pytest
+import torch
+
+from conftest import GOLDEN
+from dsmoe.synthetic import SyntheticLayer, activations
+from oracle import moe_oracle as O
+
+BLOCK_CASES = ["small_t16", "mid_t33", "tiny_t1", "c1_t8_full"]
+ROUTE_CASES = BLOCK_CASES + ["route_t512_full"]
+
+
+def load(name):
+    return torch.load(os.path.join(GOLDEN, f"{name}.pt"))
+
+
+def inputs(g):
+    layer = SyntheticLayer(g["seed"], g["layer"], g["H"], g["F"], g["E"])
+    return layer, activations(g["seed"], g["T"], g["H"])
+
+
+@pytest.mark.parametrize("name", ROUTE_CASES)
+def test_route_matches_reference_exactly(name):
+    g = load(name)
+    layer, x = inputs(g)
+    idx, w = O.route_ref(x, layer.gate, g["n_group"], g["topk_group"], g["top_k"])
+    assert torch.equal(idx, g["idx"])
+    assert torch.equal(w, g["w"])
+
+
+@pytest.mark.parametrize("name", ["small_t16", "tiny_t1", "c1_t8_full"])
+def test_literal_block_bit_exact(name):
+    g = load(name)
+    layer, x = inputs(g)
+    out, idx, _ = O.moe_block_literal(x.view(1, g["T"], g["H"]), layer.gate, layer.expert, layer.shared())
+    assert torch.equal(out.view(g["T"], -1), g["out"])
+
+
+@pytest.mark.parametrize("name", ["small_t16", "mid_t33", "tiny_t1"])
+def test_grouped_block_close(name):
+    g = load(name)
+    layer, x = inputs(g)
+    out = O.moe_block_grouped(x, g["idx"], g["w"], layer.expert, layer.shared())
+    # only the fp32 summation order of the matmul differs from the reference
+    assert O.rel_rms(out, g["out"]) < 1e-3
+
+
+def test_golden_metadata():
+    for name in ROUTE_CASES:
+        g = load(name)
+        assert g["idx"].shape == (g["T"], g["top_k"])
+        assert g["idx"].dtype == torch.int64 and g["w"].dtype == torch.float32
+        if g["kind"] == "block":
+            assert g["out"].dtype == torch.bfloat16 and g["out"].shape == (g["T"], g["H"])
+
+
+def test_route_v3_properties():
+    layer = SyntheticLayer(7, 3, 256, 128, 256, bias_zipf=1.1)
+    x = activations(7, 64, 256)
+    idx, w = O.route_v3(x, layer.gate, layer.bias)
+    assert torch.allclose(w.sum(-1), torch.full((64,), 2.5), atol=1e-5)
+    s = torch.sigmoid(O.router_logits(x, layer.gate)) + layer.bias
+    groups = (idx // 32)
+    for t in range(64):
+        assert len(set(groups[t].tolist())) <= 4
+        # chosen experts are the 8 best by biased score inside the kept groups
+        kept = set(groups[t].tolist())
+        cand = [e for e in range(256) if e // 32 in kept]
+        best = sorted(cand, key=lambda e: -float(s[t, e]))[:8]
+        assert sorted(best) == sorted(idx[t].tolist())
+
+
+def test_index_parity_tie_rule():
+    scores = torch.tensor([[0.9, 0.5, 0.5 + 5e-7, 0.1]])
+    a = torch.tensor([[0, 1]])
+    b = torch.tensor([[0, 2]])
+    bad, ties = O.index_parity(a, b, scores)
+    assert (bad, ties) == (0, 1)
+    c = torch.tensor([[0, 3]])
+    bad, ties = O.index_parity(a, c, scores)
+    assert (bad, ties) == (1, 0)
