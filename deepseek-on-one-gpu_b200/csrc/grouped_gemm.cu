@@ -25,11 +25,13 @@
 //           down GEMM's activation format.
 //   NB = 1  down: the epilogue writes y = bf16(acc) per permuted row.
 //
-// Warp roles (576 threads, one CTA per SM, persistent over work units):
+// Warp roles (320 threads, one CTA per SM, persistent over work units):
 //   warp 0      TMA producer (one thread)
 //   warp 1      TMEM allocator + MMA issuer (one thread)
-//   warps 2-17  epilogue: warp w reads TMEM lane quadrant (w % 4) and a
-//               32-column quarter ((w - 2) / 4) of every accumulator.
+//   warps 2-9   epilogue: warp w reads TMEM lane quadrant (w % 4) and a
+//               64-column half ((w - 2) / 4) of every accumulator.
+// (Registers are split over the SM's four 16K-register sub-partitions, so
+// 10 warps leave up to 168 registers per thread for the accumulators.)
 // Work unit = (group, 128-feature tile, 128-token tile); units are ordered
 // group-major, then feature tile, then token tile, so CTAs that work on the
 // token tiles of one feature tile read the same weight tile close in time.
@@ -43,7 +45,8 @@ constexpr int BM = 128;   // weight rows (output features) per tile
 constexpr int BN = 128;   // max tokens per tile
 constexpr int BK = 128;   // K bytes per stage
 constexpr int SUB = 32;   // token rows per activation TMA box
-constexpr int NUM_EPI_WARPS = 16;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int EPI_COLS = BN * 4 / NUM_EPI_WARPS;  // accumulator columns per epilogue warp
 constexpr int NUM_THREADS = (2 + NUM_EPI_WARPS) * 32;
 constexpr int MAX_GROUPS = 264;
 
@@ -81,7 +84,7 @@ __device__ __forceinline__ void decode_unit(int u, int n_groups, const int* usta
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
 
 template <int NB>
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_sx,
                     const GemmParams p) {
@@ -234,10 +237,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2;
+    // Warp w reads TMEM lane quadrant (w % 4) and the 64-column half
+    // ((w - 2) / 4) of every accumulator.
     const int quad = warp & 3;
-    const int cq = ew >> 2;
-    const int c0 = cq * 32;
+    const int ch = (warp - 2) >> 2;
+    const int c0 = ch * EPI_COLS;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     int stage = 0;
     uint32_t phase = 0;
@@ -249,7 +253,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       decode_unit(u, NG, s_ustart, s_counts, g, mt, nt, ntiles);
       const int slot = s_slot[g];
       const int ncols = min(BN, s_counts[g] - nt * BN);
-      const bool active = c0 < ncols;
+      const int nvalid = max(0, min(EPI_COLS, ncols - c0));  // valid columns of this warp
       // Weight block scales of this unit's 128-row tile, one per K block:
       // lane i holds kb = i and kb = 32 + i.
       float swr[NB][2];
@@ -263,36 +267,32 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
           swr[j][1] = slot_ok && 32 + lane < n_kb ? __ldg(ws + base + 32 + lane) : 0.f;
         }
       }
-      float acc[NB][32];
+      float acc[NB][EPI_COLS];
 #pragma unroll
       for (int j = 0; j < NB; ++j)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[j][i] = 0.f;
+        for (int i = 0; i < EPI_COLS; ++i) acc[j][i] = 0.f;
 
       for (int kb = 0; kb < n_kb; ++kb) {
         if (!mbar_wait(&tfull[tb], tphase, p.status, kDevTimeoutEpilogue, s_abort)) { ok = false; break; }
         if (!mbar_wait(&full[stage], phase, p.status, kDevTimeoutEpilogue, s_abort)) { ok = false; break; }
         tc_fence_after();
-        if (active) {
-          const float4* sx4 =
-              reinterpret_cast<const float4*>(smem + stage * C::STAGE_BYTES + C::SX_OFF) + (c0 >> 2);
+        const float4* sx4 = reinterpret_cast<const float4*>(smem + stage * C::STAGE_BYTES + C::SX_OFF) + (c0 >> 2);
+        float swj[NB];
 #pragma unroll
-          for (int j = 0; j < NB; ++j) {
-            const float swj = __shfl_sync(0xffffffffu, swr[j][kb >> 5], kb & 31);
+        for (int j = 0; j < NB; ++j) swj[j] = __shfl_sync(0xffffffffu, swr[j][kb >> 5], kb & 31);
 #pragma unroll
-            for (int hlf = 0; hlf < 2; ++hlf) {
-              float part[16];
-              tmem_ld16(tmem_base + lane_base + tb * (NB * BN) + j * BN + c0 + hlf * 16, part);
+        for (int q8 = 0; q8 < EPI_COLS / 8; ++q8) {
+          if (q8 * 8 < nvalid) {  // warp-uniform
+            const float4 s0 = sx4[q8 * 2], s1 = sx4[q8 * 2 + 1];
+            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int j = 0; j < NB; ++j) {
+              float part[8];
+              tmem_ld8(tmem_base + lane_base + tb * (NB * BN) + j * BN + c0 + q8 * 8, part);
               tmem_ld_wait();
 #pragma unroll
-              for (int i = 0; i < 16; i += 4) {
-                const float4 s = sx4[hlf * 4 + (i >> 2)];
-                float* a = &acc[j][hlf * 16 + i];
-                a[0] = fmaf(part[i + 0], s.x * swj, a[0]);
-                a[1] = fmaf(part[i + 1], s.y * swj, a[1]);
-                a[2] = fmaf(part[i + 2], s.z * swj, a[2]);
-                a[3] = fmaf(part[i + 3], s.w * swj, a[3]);
-              }
+              for (int i = 0; i < 8; ++i) acc[j][q8 * 8 + i] = fmaf(part[i], sv[i] * swj[j], acc[j][q8 * 8 + i]);
             }
           }
         }
@@ -307,67 +307,72 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         if (tb == 0) tphase ^= 1;
       }
       // A warp that gave up still takes this unit's named barriers below, so
-      // the other warps of its column quarter are not left waiting.
-      const bool store = active && ok;
+      // the other warps of its column half are not left waiting.
+      const int nstore = ok ? nvalid : 0;
 
       const int row_base = s_rows[g] + nt * BN + c0;
       const int feat = mt * BM + quad * 32 + lane;
       if constexpr (NB == 1) {
-        if (store) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (c0 + i < ncols)
-              p.y[static_cast<size_t>(row_base + i) * p.M + feat] = __float2bfloat16_rn(acc[0][i]);
-          }
+        for (int i = 0; i < EPI_COLS; ++i) {
+          if (i < nstore) p.y[static_cast<size_t>(row_base + i) * p.M + feat] = __float2bfloat16_rn(acc[0][i]);
         }
       } else {
         // h = bf16(bf16(silu(bf16(g))) * bf16(u)), then one scale per token
         // over this tile's 128 features (4 warps x 32 lanes).
-        float v[32];
-        if (store) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gt = bf16_round(silu_f32(bf16_round(acc[0][i])));
-            acc[0][i] = bf16_round(gt * bf16_round(acc[1][i]));
-            v[i] = fabsf(acc[0][i]);
-          }
-          // Transpose-reduce: afterwards lane l holds the warp max of column l.
-#pragma unroll
-          for (int w = 16; w >= 1; w >>= 1) {
-            const bool upper = (lane & w) != 0;
-#pragma unroll
-            for (int i = 0; i < w; ++i) {
-              const float send = upper ? v[i] : v[i + w];
-              const float keep = upper ? v[i + w] : v[i];
-              v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, w));
-            }
-          }
-          s_red[(cq * 4 + quad) * 32 + lane] = v[0];
+        for (int i = 0; i < EPI_COLS; ++i) {
+          const float gt = bf16_round(silu_f32(bf16_round(acc[0][i])));
+          acc[0][i] = bf16_round(gt * bf16_round(acc[1][i]));
         }
-        asm volatile("bar.sync %0, 128;" ::"r"(1 + cq) : "memory");
-        if (store) {
-          float amax = 0.f;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) amax = fmaxf(amax, s_red[(cq * 4 + q) * 32 + lane]);
-          const float inv = amax > 0.f ? 448.f / amax : 0.f;
-          const float scale = amax / 448.f;
-          uint8_t* hq_hi = p.hq;
-          uint8_t* hq_lo = p.hq + static_cast<size_t>(p.P) * p.M;
+        for (int sc = 0; sc < EPI_COLS / 32; ++sc) {
+          if (sc * 32 < nstore) {
+            float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float q = acc[0][i] * __shfl_sync(0xffffffffu, inv, i);
-            if (c0 + i < ncols) {
-              const uint16_t hi2 = f32x2_to_e4m3x2(q, 0.f);
-              const float hif = e4m3_to_f32(static_cast<uint8_t>(hi2 & 0xff));
-              const uint16_t lo2 = f32x2_to_e4m3x2(q - hif, 0.f);
-              const size_t off = static_cast<size_t>(row_base + i) * p.M + feat;
-              hq_hi[off] = static_cast<uint8_t>(hi2 & 0xff);
-              hq_lo[off] = static_cast<uint8_t>(lo2 & 0xff);
+            for (int i = 0; i < 32; ++i) v[i] = fabsf(acc[0][sc * 32 + i]);
+            // Transpose-reduce: afterwards lane l holds the warp max of column l.
+#pragma unroll
+            for (int w = 16; w >= 1; w >>= 1) {
+              const bool upper = (lane & w) != 0;
+#pragma unroll
+              for (int i = 0; i < w; ++i) {
+                const float send = upper ? v[i] : v[i + w];
+                const float keep = upper ? v[i + w] : v[i];
+                v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, w));
+              }
             }
+            s_red[((ch * 2 + sc) * 4 + quad) * 32 + lane] = v[0];
           }
-          if (quad == 0 && c0 + lane < ncols) p.hs[static_cast<size_t>(mt) * p.P + row_base + lane] = scale;
         }
-        asm volatile("bar.sync %0, 128;" ::"r"(1 + cq) : "memory");
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + ch) : "memory");
+        uint8_t* hq_hi = p.hq;
+        uint8_t* hq_lo = p.hq + static_cast<size_t>(p.P) * p.M;
+#pragma unroll
+        for (int sc = 0; sc < EPI_COLS / 32; ++sc) {
+          if (sc * 32 < nstore) {
+            float amax = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) amax = fmaxf(amax, s_red[((ch * 2 + sc) * 4 + q) * 32 + lane]);
+            const float inv = amax > 0.f ? 448.f / amax : 0.f;
+            const float scale = amax / 448.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float q = acc[0][sc * 32 + i] * __shfl_sync(0xffffffffu, inv, i);
+              if (sc * 32 + i < nstore) {
+                const uint16_t hi2 = f32x2_to_e4m3x2(q, 0.f);
+                const float hif = e4m3_to_f32(static_cast<uint8_t>(hi2 & 0xff));
+                const uint16_t lo2 = f32x2_to_e4m3x2(q - hif, 0.f);
+                const size_t off = static_cast<size_t>(row_base + sc * 32 + i) * p.M + feat;
+                hq_hi[off] = static_cast<uint8_t>(hi2 & 0xff);
+                hq_lo[off] = static_cast<uint8_t>(lo2 & 0xff);
+              }
+            }
+            if (quad == 0 && sc * 32 + lane < nstore)
+              p.hs[static_cast<size_t>(mt) * p.P + row_base + sc * 32 + lane] = scale;
+          }
+        }
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + ch) : "memory");
       }
       if (!ok) break;
     }

@@ -151,13 +151,14 @@ def test_moe_block_all_tokens_one_expert_set():
     store = SyntheticWeightStore(cfg, seed=4, device=DEV, pin_memory=False, gen_device="cpu")
     L = store.layer(3)
     gate = torch.zeros(256, H)
-    gate[[3, 40, 77, 100, 130, 170, 200, 250]] = 0.05
+    chosen = [3, 5, 10, 20, 40, 41, 50, 60]  # groups 0 and 1 only: both survive the top-4 group cut
+    gate[chosen] = 0.05
     gate = gate.to(torch.bfloat16)
     store._gate[3] = gate.to(DEV)
     x = activations(4, T, H).abs()
     gt = GPUTransfer(cfg, store, DEV)
     out, idx, w = moe_block(x.to(DEV), 3, store, gt, cfg, return_routing=True)
-    assert set(idx.unique().tolist()) == {3, 40, 77, 100, 130, 170, 200, 250}
+    assert set(idx.unique().tolist()) == set(chosen)
     idx_r, w_r = O.route_ref(x, gate)
     ref = O.moe_block_grouped(x, idx_r, w_r, L.expert, L.shared())
     assert O.rel_rms(out.float().cpu(), ref.float()) < REL_RMS_TOL
