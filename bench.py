@@ -165,6 +165,8 @@ def main():
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--ref-tokens-per-step", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=E, help="routed experts (32 per group); smaller = profiling case")
+    ap.add_argument("--skip-e2e", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -189,7 +191,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     T = args.tokens
-    cfg = DeepSeekConfig()
+    n_group = max(1, args.experts // 32)
+    cfg = DeepSeekConfig(n_routed_experts=32 * n_group, n_group=n_group, topk_group=min(4, n_group))
     store = SyntheticWeightStore(cfg, seed=1 + rank, device=dev, pin_memory=False, gen_device="cuda")
     gt = GPUTransfer(cfg, store, dev)
     bank = gt.bank(LAYER)
@@ -226,41 +229,47 @@ def main():
     value = world * T / (ms_max / 1000.0)
 
     # ------------------------------------------------- per-stage (roofline)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
     set_profile_events(evs)
-    stage_ms = [0.0] * 5
+    names = ["router", "permute", "gate_up", "swiglu_quant", "down", "combine"]
+    stage_ms = [0.0] * len(names)
     n_prof = max(3, args.steps // 2)
     for _ in range(n_prof):
         out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)
         torch.cuda.synchronize()
-        for i in range(5):
+        for i in range(len(names)):
             stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
     set_profile_events(None)
-    counts = torch.bincount(idx.reshape(-1), minlength=E).cpu()
+    counts = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).cpu()
     touched = int((counts > 0).sum()) + 1  # + shared expert
     rows = T * TOPK + T
     w13 = 2 * F * H + 2 * (F // 128) * (H // 128) * 4
     w2 = F * H + (F // 128) * (H // 128) * 4
-    gateup_bytes = touched * w13 + rows * H * 2 + rows * (H // 128) * 4 + rows * F * 2 + rows * (F // 128) * 4
-    down_bytes = touched * w2 + rows * F * 2 + rows * (F // 128) * 4 + rows * H * 2
+    # algorithmic bytes per launch: weights of every expert used, activations
+    # read once per (token, expert) row (hi + lo = 2 B/element + scales), outputs
+    gateup_bytes = touched * w13 + rows * (H * 2 + (H // 128) * 4) + rows * 2 * F * 2
+    swiglu_bytes = rows * 2 * F * 2 + rows * (F * 2 + (F // 128) * 4)
+    down_bytes = touched * w2 + rows * (F * 2 + (F // 128) * 4) + rows * H * 2
     algo_flops = 2.0 * rows * 3 * F * H  # useful FP8-GEMM work (hi/lo doubles what the tensor pipe executes)
     hbm_peak, bf16_peak, peak_src = peaks()
-    gu_ms, dn_ms = stage_ms[2], stage_ms[3]
+    gu_ms, dn_ms = stage_ms[2], stage_ms[4]
     dominant = "gate_up" if gu_ms >= dn_ms else "down"
     dom_bytes, dom_ms = (gateup_bytes, gu_ms) if dominant == "gate_up" else (down_bytes, dn_ms)
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
-    roofline = {"kernel": f"grouped_gemm_kernel<{2 if dominant == 'gate_up' else 1}> ({dominant})",
+    roofline = {"kernel": f"grouped_gemm_kernel ({dominant})",
                 "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": achieved / hbm_peak, "peak_source": peak_src, "traffic": None,
                 "algorithmic_bytes_per_launch": dom_bytes}
-    layer_bytes = gateup_bytes + down_bytes
+    layer_bytes = gateup_bytes + swiglu_bytes + down_bytes
     layer_ms = sum(stage_ms)
 
     # ------------------------------------------------------------------ e2e
+    if args.skip_e2e:
+        args.steps_e2e = 0
     x_host = x.cpu().pin_memory()
     out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
     x_in = torch.empty_like(x)
-    for _ in range(3):
+    for _ in range(0 if args.skip_e2e else 3):
         x_in.copy_(x_host, non_blocking=True)
         out_host.copy_(step(x_in), non_blocking=True)
     torch.cuda.synchronize()
@@ -268,12 +277,12 @@ def main():
         dist.barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record()
-    for _ in range(args.steps):
+    for _ in range(1 if args.skip_e2e else args.steps):
         x_in.copy_(x_host, non_blocking=True)
         out_host.copy_(step(x_in), non_blocking=True)
     e3.record()
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e2.elapsed_time(e3) / args.steps], device=dev)
+    e2e_ms = torch.tensor([e2.elapsed_time(e3) / (1 if args.skip_e2e else args.steps)], device=dev)
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = world * T / (float(e2e_ms.item()) / 1000.0)
@@ -304,22 +313,22 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) FP8 block-quantised experts)",
-            "config": {"workload": f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, 256+1 experts "
-                                   f"resident (config 2)" + ("; replicas per rank" if world > 1 else ""),
-                       "tokens_per_gpu": T, "hidden": H, "moe_intermediate": F, "experts": E, "top_k": TOPK,
+            "config": {"workload": f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, "
+                                   f"{cfg.n_routed_experts}+1 experts resident (config 2)"
+                                   + ("; replicas per rank" if world > 1 else ""),
+                       "tokens_per_gpu": T, "hidden": H, "moe_intermediate": F, "experts": cfg.n_routed_experts, "top_k": TOPK,
                        "router": "ref", "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
                        "parallelism": f"replica x{world}" if world > 1 else "single GPU"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},
             "roofline": roofline,
-            "stages_ms": {"router": stage_ms[0], "permute": stage_ms[1], "gate_up": gu_ms, "down": dn_ms,
-                          "combine": stage_ms[4]},
+            "stages_ms": dict(zip(names, stage_ms)),
             "layer": {"algorithmic_bytes": layer_bytes, "GB_s": layer_bytes / (layer_ms / 1e3) / 1e9,
                       "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm_peak,
                       "fp8_tflops_algorithmic": algo_flops / (ms_max / 1e3) / 1e12,
                       "fp8_frac_of_nominal_dense": algo_flops / (ms_max / 1e3) / 1e12 / FP8_DENSE_NOMINAL_TFLOPS,
                       "experts_touched": touched},
-            "gpu_launches": 8 * args.steps,
+            "gpu_launches": 9 * args.steps,
             "device_status": status,
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -97,7 +97,7 @@ int num_sms() {
 // --------------------------------------------------------------- workspace
 struct Ws {
   size_t status = 0, counts = 0, cursor = 0, row_start = 0, us_up = 0, us_dn = 0, slot0 = 0;
-  size_t partial = 0, idx = 0, w = 0, pos = 0, xq = 0, sx = 0, hq = 0, hs = 0, y = 0, total = 0;
+  size_t partial = 0, idx = 0, w = 0, pos = 0, xq = 0, sx = 0, gu = 0, hq = 0, hs = 0, y = 0, total = 0;
   int P = 0, ksplit = 1, NG = 1;
 };
 
@@ -124,9 +124,10 @@ Ws plan_moe(int T, int H, int F, int E, int K) {
   w.w = take(4 * static_cast<size_t>(pairs));
   w.pos = take(4 * static_cast<size_t>(pairs));
   w.xq = take(2 * static_cast<size_t>(w.P) * H);
-  w.sx = take(4 * static_cast<size_t>(H / 128) * w.P);
+  w.sx = take(4 * static_cast<size_t>(w.P));
+  w.gu = take(2 * static_cast<size_t>(w.P) * 2 * F);
   w.hq = take(2 * static_cast<size_t>(w.P) * F);
-  w.hs = take(4 * static_cast<size_t>(F / 128) * w.P);
+  w.hs = take(4 * static_cast<size_t>(w.P));
   w.y = take(2 * static_cast<size_t>(w.P) * H);
   w.total = o;
   return w;
@@ -147,10 +148,11 @@ Ws plan_single(int T, int K_in, int F /* 0 for a plain linear */) {
   w.us_dn = take(4 * 2);
   w.slot0 = take(4);
   w.xq = take(2 * static_cast<size_t>(w.P) * K_in);
-  w.sx = take(4 * static_cast<size_t>(K_in / 128) * w.P);
+  w.sx = take(4 * static_cast<size_t>(w.P));
   if (F > 0) {
+    w.gu = take(2 * static_cast<size_t>(w.P) * 2 * F);
     w.hq = take(2 * static_cast<size_t>(w.P) * F);
-    w.hs = take(4 * static_cast<size_t>(F / 128) * w.P);
+    w.hs = take(4 * static_cast<size_t>(w.P));
   }
   w.total = o;
   return w;
@@ -206,6 +208,101 @@ int check_weights(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* w) {
   return DSMOE_OK;
 }
 
+
+// One grouped-GEMM launch: TMA descriptors for the weight bank(s), the hi/lo
+// activation rows and their scales, then the persistent kernel.
+struct GemmJob {
+  const void* w0;
+  const void* w1;       // second matrix (gate/up), else == w0
+  const float* s0;
+  const float* s1;
+  int n_mat, M, K, n_slots;
+  const uint8_t* xq;    // [2P][K] e4m3
+  const float* sx;      // [P] per-row scales
+  int P;
+  const int32_t *counts, *row_start, *unit_start, *slot_of;
+  int n_groups;
+  __nv_bfloat16* y;     // [P][n_mat * M]
+  int* status;
+};
+
+int run_gemm(const GemmJob& j, cudaStream_t s) {
+  CUtensorMap m_w0, m_w1, m_x, m_x32;
+  const uint64_t rows = static_cast<uint64_t>(j.n_slots) * j.M;
+  int r;
+  if ((r = make_map(&m_w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.w0, j.K, rows, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return r;
+  if ((r = make_map(&m_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.w1, j.K, rows, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return r;
+  if ((r = make_map(&m_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.xq, j.K, 2ull * j.P, 128, GEMM_BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B)))
+    return r;
+  if ((r = make_map(&m_x32, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.xq, j.K, 2ull * j.P, 128, 32,
+                    CU_TENSOR_MAP_SWIZZLE_128B)))
+    return r;
+  GemmParams gp{};
+  gp.counts = j.counts;
+  gp.row_start = j.row_start;
+  gp.unit_start = j.unit_start;
+  gp.slot_of = j.slot_of;
+  gp.wscale0 = j.s0;
+  gp.wscale1 = j.s1;
+  gp.n_groups = j.n_groups;
+  gp.n_slots = j.n_slots;
+  gp.n_mat = j.n_mat;
+  gp.M = j.M;
+  gp.K = j.K;
+  gp.P = j.P;
+  gp.sx = j.sx;
+  gp.y = j.y;
+  gp.status = j.status;
+  DSMOE_CUDA(launch_grouped_gemm(m_w0, m_w1, m_x, m_x32, gp, num_sms(), s));
+  return DSMOE_OK;
+}
+
+// Gate/up GEMM -> SwiGLU + hi/lo split -> down GEMM, for any group table.
+int run_ffn(const void* w_gate, const float* s_gate, const void* w_up, const float* s_up, const void* w_down,
+            const float* s_down, int n_slots, int H, int F, const Ws& L, void* ws, const int32_t* slot_of,
+            int n_groups, __nv_bfloat16* y, cudaStream_t s) {
+  GemmJob j{};
+  j.n_slots = n_slots;
+  j.P = L.P;
+  j.counts = at<int32_t>(ws, L.counts);
+  j.row_start = at<int32_t>(ws, L.row_start);
+  j.slot_of = slot_of;
+  j.n_groups = n_groups;
+  j.status = at<int>(ws, L.status);
+  int r;
+  j.w0 = w_gate;
+  j.w1 = w_up;
+  j.s0 = s_gate;
+  j.s1 = s_up;
+  j.n_mat = 2;
+  j.M = F;
+  j.K = H;
+  j.xq = at<uint8_t>(ws, L.xq);
+  j.sx = at<float>(ws, L.sx);
+  j.unit_start = at<int32_t>(ws, L.us_up);
+  j.y = at<__nv_bfloat16>(ws, L.gu);
+  if ((r = run_gemm(j, s))) return r;
+  prof(3, s);
+  DSMOE_CUDA(launch_swiglu_quant(at<__nv_bfloat16>(ws, L.gu), F, at<int32_t>(ws, L.row_start) + n_groups, L.P,
+                                 at<uint8_t>(ws, L.hq), at<float>(ws, L.hs), s));
+  prof(4, s);
+  j.w0 = j.w1 = w_down;
+  j.s0 = j.s1 = s_down;
+  j.n_mat = 1;
+  j.M = H;
+  j.K = F;
+  j.xq = at<uint8_t>(ws, L.hq);
+  j.sx = at<float>(ws, L.hs);
+  j.unit_start = at<int32_t>(ws, L.us_dn);
+  j.y = y;
+  if ((r = run_gemm(j, s))) return r;
+  prof(5, s);
+  return DSMOE_OK;
+}
+
 // Permute + both grouped GEMMs + combine, routing already in the workspace.
 int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, const void* hidden, int T, void* out,
                const Ws& L, void* ws, cudaStream_t s) {
@@ -216,72 +313,24 @@ int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, con
   int32_t* us_up = at<int32_t>(ws, L.us_up);
   int32_t* us_dn = at<int32_t>(ws, L.us_dn);
   int32_t* idx = at<int32_t>(ws, L.idx);
-  uint8_t* xq = at<uint8_t>(ws, L.xq);
-  float* sx = at<float>(ws, L.sx);
-  uint8_t* hq = at<uint8_t>(ws, L.hq);
-  float* hs = at<float>(ws, L.hs);
   __nv_bfloat16* y = at<__nv_bfloat16>(ws, L.y);
   int32_t* pos = at<int32_t>(ws, L.pos);
 
   DSMOE_CUDA(launch_count(idx, T * K, counts, NG, s));
-  DSMOE_CUDA(launch_plan(counts, NG, T, F / 128, H / 128, row_start, cursor, us_up, us_dn, nullptr, s));
-  DSMOE_CUDA(launch_quant_scatter(hidden, T, H, idx, K, 1, row_start, cursor, L.P, xq, sx, pos, s));
+  DSMOE_CUDA(launch_plan(counts, NG, T, 2 * F / 128, H / 128, row_start, cursor, us_up, us_dn, s));
+  DSMOE_CUDA(launch_quant_scatter(hidden, T, H, idx, K, 1, row_start, cursor, L.P, at<uint8_t>(ws, L.xq),
+                                  at<float>(ws, L.sx), pos, s));
   prof(2, s);
 
-  CUtensorMap m_w1, m_w3, m_w2, m_x, m_sx, m_h, m_hs;
   int r;
-  const uint64_t ns = static_cast<uint64_t>(wt->n_slots);
-  if ((r = make_map(&m_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, wt->w_gate, H, ns * F, 128, 128,
-                    CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((r = run_ffn(wt->w_gate, wt->s_gate, wt->w_up, wt->s_up, wt->w_down, wt->s_down, wt->n_slots, H, F, L, ws,
+                   wt->slot_of_expert, NG, y, s)))
     return r;
-  if ((r = make_map(&m_w3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, wt->w_up, H, ns * F, 128, 128,
-                    CU_TENSOR_MAP_SWIZZLE_128B)))
-    return r;
-  if ((r = make_map(&m_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, wt->w_down, F, ns * H, 128, 128,
-                    CU_TENSOR_MAP_SWIZZLE_128B)))
-    return r;
-  if ((r = make_map(&m_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xq, H, 2ull * L.P, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
-    return r;
-  if ((r = make_map(&m_sx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, sx, L.P, H / 128, 128, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
-    return r;
-  if ((r = make_map(&m_h, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hq, F, 2ull * L.P, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
-    return r;
-  if ((r = make_map(&m_hs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, hs, L.P, F / 128, 128, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
-    return r;
-
-  GemmParams gp{};
-  gp.counts = counts;
-  gp.row_start = row_start;
-  gp.slot_of = wt->slot_of_expert;
-  gp.n_groups = NG;
-  gp.n_slots = wt->n_slots;
-  gp.P = L.P;
-  gp.status = at<int>(ws, L.status);
-  const int grid = num_sms();
-
-  gp.unit_start = us_up;
-  gp.wscale0 = wt->s_gate;
-  gp.wscale1 = wt->s_up;
-  gp.M = F;
-  gp.K = H;
-  gp.hq = hq;
-  gp.hs = hs;
-  DSMOE_CUDA(launch_grouped_gemm(2, m_w1, m_w3, m_x, m_sx, gp, grid, s));
-  prof(3, s);
-
-  gp.unit_start = us_dn;
-  gp.wscale0 = wt->s_down;
-  gp.wscale1 = wt->s_down;
-  gp.M = H;
-  gp.K = F;
-  gp.y = y;
-  DSMOE_CUDA(launch_grouped_gemm(1, m_w2, m_w2, m_h, m_hs, gp, grid, s));
-  prof(4, s);
 
   const float scale = c->router_mode == DSMOE_ROUTER_V3 ? 1.0f : c->routed_scaling_factor;
   DSMOE_CUDA(launch_combine(y, T, H, pos, at<float>(ws, L.w), K, row_start, scale,
                             static_cast<__nv_bfloat16*>(out), s));
-  prof(5, s);
+  prof(6, s);
   return DSMOE_OK;
 }
 
@@ -370,7 +419,7 @@ static int single_prologue(const void* x, int T, int K_in, int mt_up, int mt_dn,
                            cudaStream_t s) {
   DSMOE_CUDA(cudaMemsetAsync(at<int32_t>(ws, L.slot0), 0, 4, s));
   DSMOE_CUDA(launch_plan(at<int32_t>(ws, L.counts), 1, T, mt_up, mt_dn, at<int32_t>(ws, L.row_start),
-                         at<int32_t>(ws, L.cursor), at<int32_t>(ws, L.us_up), at<int32_t>(ws, L.us_dn), nullptr, s));
+                         at<int32_t>(ws, L.cursor), at<int32_t>(ws, L.us_up), at<int32_t>(ws, L.us_dn), s));
   DSMOE_CUDA(launch_quant_scatter(x, T, K_in, nullptr, 0, 1, at<int32_t>(ws, L.row_start),
                                   at<int32_t>(ws, L.cursor), L.P, at<uint8_t>(ws, L.xq), at<float>(ws, L.sx), nullptr,
                                   s));
@@ -393,43 +442,10 @@ int dsmoe_expert_ffn(const void* x, int32_t tokens, int32_t hidden, int32_t inte
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int r;
   int32_t* counts = at<int32_t>(workspace, L.counts);
-  if ((r = single_prologue(x, tokens, hidden, inter / 128, hidden / 128, L, workspace, s))) return r;
-  CUtensorMap m_w1, m_w3, m_w2, m_x, m_sx, m_h, m_hs;
-  if ((r = make_map(&m_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w_gate, hidden, inter, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))) return r;
-  if ((r = make_map(&m_w3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w_up, hidden, inter, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))) return r;
-  if ((r = make_map(&m_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w_down, inter, hidden, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))) return r;
-  if ((r = make_map(&m_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, at<uint8_t>(workspace, L.xq), hidden, 2ull * L.P, 128, 32,
-                    CU_TENSOR_MAP_SWIZZLE_128B))) return r;
-  if ((r = make_map(&m_sx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, at<float>(workspace, L.sx), L.P, hidden / 128, 128, 1,
-                    CU_TENSOR_MAP_SWIZZLE_NONE))) return r;
-  if ((r = make_map(&m_h, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, at<uint8_t>(workspace, L.hq), inter, 2ull * L.P, 128, 32,
-                    CU_TENSOR_MAP_SWIZZLE_128B))) return r;
-  if ((r = make_map(&m_hs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, at<float>(workspace, L.hs), L.P, inter / 128, 128, 1,
-                    CU_TENSOR_MAP_SWIZZLE_NONE))) return r;
-  GemmParams gp{};
-  gp.counts = counts;
-  gp.row_start = at<int32_t>(workspace, L.row_start);
-  gp.slot_of = at<int32_t>(workspace, L.slot0);
-  gp.n_groups = 1;
-  gp.n_slots = 1;
-  gp.P = L.P;
-  gp.status = at<int>(workspace, L.status);
-  const int grid = num_sms();
-  gp.unit_start = at<int32_t>(workspace, L.us_up);
-  gp.wscale0 = s_gate;
-  gp.wscale1 = s_up;
-  gp.M = inter;
-  gp.K = hidden;
-  gp.hq = at<uint8_t>(workspace, L.hq);
-  gp.hs = at<float>(workspace, L.hs);
-  DSMOE_CUDA(launch_grouped_gemm(2, m_w1, m_w3, m_x, m_sx, gp, grid, s));
-  gp.unit_start = at<int32_t>(workspace, L.us_dn);
-  gp.wscale0 = s_down;
-  gp.wscale1 = s_down;
-  gp.M = hidden;
-  gp.K = inter;
-  gp.y = static_cast<__nv_bfloat16*>(out);
-  DSMOE_CUDA(launch_grouped_gemm(1, m_w2, m_w2, m_h, m_hs, gp, grid, s));
+  if ((r = single_prologue(x, tokens, hidden, 2 * inter / 128, hidden / 128, L, workspace, s))) return r;
+  if ((r = run_ffn(w_gate, s_gate, w_up, s_up, w_down, s_down, 1, hidden, inter, L, workspace,
+                   at<int32_t>(workspace, L.slot0), 1, static_cast<__nv_bfloat16*>(out), s)))
+    return r;
   return DSMOE_OK;
 }
 
@@ -450,29 +466,24 @@ int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_features, int32_t
   int r;
   int32_t* counts = at<int32_t>(workspace, L.counts);
   if ((r = single_prologue(x, tokens, in_features, 0, out_features / 128, L, workspace, s))) return r;
-  CUtensorMap m_w, m_x, m_sx;
-  if ((r = make_map(&m_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, weight, in_features, out_features, 128, 128,
-                    CU_TENSOR_MAP_SWIZZLE_128B))) return r;
-  if ((r = make_map(&m_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, at<uint8_t>(workspace, L.xq), in_features, 2ull * L.P,
-                    128, 32, CU_TENSOR_MAP_SWIZZLE_128B))) return r;
-  if ((r = make_map(&m_sx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, at<float>(workspace, L.sx), L.P, in_features / 128,
-                    128, 1, CU_TENSOR_MAP_SWIZZLE_NONE))) return r;
-  GemmParams gp{};
-  gp.counts = counts;
-  gp.row_start = at<int32_t>(workspace, L.row_start);
-  gp.slot_of = at<int32_t>(workspace, L.slot0);
-  gp.n_groups = 1;
-  gp.n_slots = 1;
-  gp.P = L.P;
-  gp.status = at<int>(workspace, L.status);
-  gp.unit_start = at<int32_t>(workspace, L.us_dn);
-  gp.wscale0 = scale_inv;
-  gp.wscale1 = scale_inv;
-  gp.M = out_features;
-  gp.K = in_features;
-  gp.y = static_cast<__nv_bfloat16*>(out);
-  DSMOE_CUDA(launch_grouped_gemm(1, m_w, m_w, m_x, m_sx, gp, num_sms(), s));
-  return DSMOE_OK;
+  GemmJob j{};
+  j.w0 = j.w1 = weight;
+  j.s0 = j.s1 = scale_inv;
+  j.n_mat = 1;
+  j.M = out_features;
+  j.K = in_features;
+  j.n_slots = 1;
+  j.xq = at<uint8_t>(workspace, L.xq);
+  j.sx = at<float>(workspace, L.sx);
+  j.P = L.P;
+  j.counts = counts;
+  j.row_start = at<int32_t>(workspace, L.row_start);
+  j.unit_start = at<int32_t>(workspace, L.us_dn);
+  j.slot_of = at<int32_t>(workspace, L.slot0);
+  j.n_groups = 1;
+  j.y = static_cast<__nv_bfloat16*>(out);
+  j.status = at<int>(workspace, L.status);
+  return run_gemm(j, s);
 }
 
 int dsmoe_read_status(void* workspace, int32_t* device_status, dsmoe_stream_t stream) {

@@ -8,6 +8,11 @@
 
 namespace dsmoe {
 
+// Token tile of the grouped GEMM (max tokens per work unit) and its pipeline
+// depth; the unit plan (permute.cu) counts tiles of the same size.
+constexpr int GEMM_BN = 192;
+constexpr int GEMM_STAGES = 3;
+
 // Group-table convention used by every kernel: group 0 is the shared expert
 // (every token, in token order), group 1 + e is routed expert e.
 struct GemmParams {
@@ -15,22 +20,27 @@ struct GemmParams {
   const int32_t* row_start;   // [n_groups] first permuted row (multiple of 32)
   const int32_t* unit_start;  // [n_groups + 1] prefix sum of work units
   const int32_t* slot_of;     // [n_groups] weight-bank slot of each group
-  const float* wscale0;       // [n_slots][M/128][K/128]
-  const float* wscale1;       // second weight (gate/up only)
+  const float* wscale0;       // [n_slots][M/128][K/128] scales of weight matrix 0
+  const float* wscale1;       // same for matrix 1 (n_mat == 2)
   int n_groups;
   int n_slots;
-  int M;  // weight rows per expert (output features)
-  int K;  // reduction length
-  int P;  // rows of one activation half (hi rows [0,P), lo rows [P,2P))
-  uint8_t* hq;          // gate/up output: e4m3 [2P][M]
-  float* hs;            // gate/up output scales: [M/128][P]
-  __nv_bfloat16* y;     // down output: bf16 [P][M]
+  int n_mat;  // weight matrices per launch: 2 = gate and up, 1 = down / single linear
+  int M;      // rows of one weight matrix per expert (output features)
+  int K;      // reduction length
+  int P;      // rows of one activation half (hi rows [0,P), lo rows [P,2P))
+  const float* sx;      // [P] per-row activation scale
+  __nv_bfloat16* y;     // output: bf16 [P][n_mat * M]
   int* status;          // device error word
 };
 
-int gemm_smem_bytes(int nb);
-cudaError_t launch_grouped_gemm(int nb, const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
-                                const CUtensorMap& sx, const GemmParams& p, int grid, cudaStream_t stream);
+int gemm_tile_tokens();
+// x: activation map with GEMM_BN-row boxes, x32: the same rows with 32-row boxes.
+cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
+                                const CUtensorMap& x32, const GemmParams& p, int grid, cudaStream_t stream);
+
+// SwiGLU + hi/lo split (swiglu_quant.cu)
+cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_end, int P, uint8_t* hq,
+                                float* hs, cudaStream_t stream);
 
 // Router (router.cu)
 int router_ksplit(int T, int H, int E, int num_sms);
@@ -43,7 +53,7 @@ cudaError_t launch_router_select(const float* partial, int ksplit, const float* 
 // Permutation (permute.cu)
 cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream);
 cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int mt_up, int mt_dn, int32_t* row_start,
-                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, int32_t* bad, cudaStream_t stream);
+                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, cudaStream_t stream);
 cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int has_shared,
                                  const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq, float* sx,
                                  int32_t* pos, cudaStream_t stream);

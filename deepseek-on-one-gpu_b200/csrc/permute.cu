@@ -8,12 +8,14 @@
 //           of both GEMMs (one block)
 //   scatter one warp per token: claims one row in each of its experts'
 //           segments (+ its row in the shared-expert segment), splits the bf16
-//           row into hi/lo e4m3 terms with one fp32 scale per 128 columns,
-//           writes the row copies and records the (token, k) -> row map used
-//           by the combine.
-// Activation format (per row r, 128-column block b):
+//           row into hi/lo e4m3 terms with one fp32 scale per row, writes the
+//           row copies and records the (token, k) -> row map used by the
+//           combine.
+// Activation format (per row r):
 //   sx = amax / 448;  q = x * 448 / amax;  hi = e4m3(q);  lo = e4m3(q - hi)
-//   x ~= (hi + lo) * sx   (about 8 significant bits instead of 4).
+//   x ~= (hi + lo) * sx   (about 8 significant bits instead of 4; one scale
+//   per row gives the same error as one per 128 columns, and lets the GEMM
+//   apply it once after the K loop).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -65,7 +67,7 @@ __global__ void __launch_bounds__(MAX_GROUPS) plan_kernel(int32_t* __restrict__ 
   if (i < n_groups) c = i == 0 ? shared_tokens : counts[i];
   __syncthreads();
   if (i == 0) counts[0] = shared_tokens;
-  const int nt = (c + 127) / 128;
+  const int nt = (c + GEMM_BN - 1) / GEMM_BN;
   const int seg = block_excl_scan<MAX_GROUPS>((c + 31) & ~31, buf);
   const int uu = block_excl_scan<MAX_GROUPS>(mt_up * nt, buf);
   const int ud = block_excl_scan<MAX_GROUPS>(mt_dn * nt, buf);
@@ -101,56 +103,53 @@ __global__ void __launch_bounds__(256) quant_scatter_kernel(const __nv_bfloat16*
     if (k < top_k) rows[has_shared + k] = r;
   }
   n += top_k;
-  const int nblk = H / 128;
-  const int iters = (nblk + 1) / 2;
   const __nv_bfloat16* xr = x + static_cast<size_t>(t) * H;
   uint8_t* xq_lo = xq + static_cast<size_t>(P) * H;
-  for (int it = 0; it < iters; ++it) {
-    const int blk = it * 2 + (lane >> 4);
-    const bool active = blk < nblk;
-    const int col = blk * 128 + (lane & 15) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (active) v = __ldg(reinterpret_cast<const uint4*>(xr + col));
+  // pass 1: row amax (each lane covers 8 consecutive columns per 256)
+  float amax = 0.f;
+  for (int col = lane * 8; col < H; col += 256) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + col));
     const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
-    float f[8];
-    float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      f[i] = __bfloat162float(vb[i]);
-      amax = fmaxf(amax, fabsf(f[i]));
-    }
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(vb[i])));
+  }
 #pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float inv = amax > 0.f ? 448.f / amax : 0.f;
-    const float scale = amax / 448.f;
+  for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float inv = amax > 0.f ? 448.f / amax : 0.f;
+  if (lane < n) {
+    int rr = rows[0];
+#pragma unroll
+    for (int r = 1; r < 9; ++r)
+      if (r == lane) rr = rows[r];
+    sx[rr] = amax / 448.f;
+  }
+  // pass 2: split and write every copy of the row
+  for (int col = lane * 8; col < H; col += 256) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + col));
+    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
     uint32_t hw[2], lw[2];
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
-      const float q0 = f[i] * inv, q1 = f[i + 1] * inv;
+      const float q0 = __bfloat162float(vb[i]) * inv, q1 = __bfloat162float(vb[i + 1]) * inv;
       const uint16_t h2 = f32x2_to_e4m3x2(q0, q1);
-      const float h0 = e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff));
-      const float h1 = e4m3_to_f32(static_cast<uint8_t>(h2 >> 8));
-      const uint16_t l2 = f32x2_to_e4m3x2(q0 - h0, q1 - h1);
-      const int w = i >> 2, sh = (i & 2) * 8;
-      if (sh == 0) {
-        hw[w] = h2;
-        lw[w] = l2;
+      const uint16_t l2 = f32x2_to_e4m3x2(q0 - e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff)),
+                                          q1 - e4m3_to_f32(static_cast<uint8_t>(h2 >> 8)));
+      if ((i & 2) == 0) {
+        hw[i >> 2] = h2;
+        lw[i >> 2] = l2;
       } else {
-        hw[w] |= static_cast<uint32_t>(h2) << 16;
-        lw[w] |= static_cast<uint32_t>(l2) << 16;
+        hw[i >> 2] |= static_cast<uint32_t>(h2) << 16;
+        lw[i >> 2] |= static_cast<uint32_t>(l2) << 16;
       }
     }
-    if (active) {
-      const uint2 hv = make_uint2(hw[0], hw[1]);
-      const uint2 lv = make_uint2(lw[0], lw[1]);
+    const uint2 hv = make_uint2(hw[0], hw[1]);
+    const uint2 lv = make_uint2(lw[0], lw[1]);
 #pragma unroll
-      for (int r = 0; r < 9; ++r) {
-        if (r < n) {
-          const size_t off = static_cast<size_t>(rows[r]) * H + col;
-          *reinterpret_cast<uint2*>(xq + off) = hv;
-          *reinterpret_cast<uint2*>(xq_lo + off) = lv;
-          if ((lane & 15) == 0) sx[static_cast<size_t>(blk) * P + rows[r]] = scale;
-        }
+    for (int r = 0; r < 9; ++r) {
+      if (r < n) {
+        const size_t off = static_cast<size_t>(rows[r]) * H + col;
+        *reinterpret_cast<uint2*>(xq + off) = hv;
+        *reinterpret_cast<uint2*>(xq_lo + off) = lv;
       }
     }
   }
@@ -169,7 +168,7 @@ cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n
 }
 
 cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int mt_up, int mt_dn, int32_t* row_start,
-                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, int32_t*, cudaStream_t stream) {
+                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, cudaStream_t stream) {
   if (n_groups + 1 > pm::MAX_GROUPS) return cudaErrorInvalidValue;
   pm::plan_kernel<<<1, pm::MAX_GROUPS, 0, stream>>>(counts, n_groups, shared_tokens, mt_up, mt_dn, row_start, cursor,
                                                     ustart_up, ustart_dn);

@@ -50,7 +50,8 @@ __global__ void __launch_bounds__(256) logits_kernel(const __nv_bfloat16* __rest
   for (int k0 = kbeg; k0 < kend; k0 += BKR) {
     uint4 xv = make_uint4(0, 0, 0, 0);
     if (t0 + lr < T) xv = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + lr) * H + k0 + lk));
-    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gw + static_cast<size_t>(e0 + lr) * H + k0 + lk));
+    uint4 gv = make_uint4(0, 0, 0, 0);
+    if (e0 + lr < E) gv = __ldg(reinterpret_cast<const uint4*>(gw + static_cast<size_t>(e0 + lr) * H + k0 + lk));
     const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
     const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv);
     __syncthreads();
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(256) logits_kernel(const __nv_bfloat16* __rest
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int t = t0 + ty * 4 + i;
-    if (t < T)
+    if (t < T && e0 + tx * 4 < E)
       *reinterpret_cast<float4*>(partial + (static_cast<size_t>(ks) * T + t) * E + e0 + tx * 4) =
           make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   }
@@ -204,7 +205,8 @@ __global__ void __launch_bounds__(256) select_kernel(const float* __restrict__ p
 
 int router_ksplit(int T, int H, int E, int num_sms) {
   const int k_tiles = H / rt::BKR;
-  const int base = ((T + rt::BT - 1) / rt::BT) * (E / rt::BE);
+  const int base = ((T + rt::BT - 1) / rt::BT) * ((E + rt::BE - 1) / rt::BE);
+  if (base <= 0) return 1;
   int want = (2 * num_sms + base - 1) / base;
   if (want < 1) want = 1;
   int best = 1;
@@ -216,7 +218,7 @@ int router_ksplit(int T, int H, int E, int num_sms) {
 cudaError_t launch_router_logits(const void* x, const void* gate, float* partial, int T, int H, int E, int ksplit,
                                  cudaStream_t stream) {
   const int kps = (H / rt::BKR / ksplit) * rt::BKR;
-  dim3 grid((T + rt::BT - 1) / rt::BT, E / rt::BE, ksplit);
+  dim3 grid((T + rt::BT - 1) / rt::BT, (E + rt::BE - 1) / rt::BE, ksplit);
   rt::logits_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
                                               static_cast<const __nv_bfloat16*>(gate), partial, T, H, E, kps);
   return cudaGetLastError();

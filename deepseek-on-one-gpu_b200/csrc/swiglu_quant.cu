@@ -1,0 +1,83 @@
+// SwiGLU + FP8 hi/lo split of the down-projection input.
+//
+// For every permuted row r (one (token, expert) pair) the gate/up GEMM left
+// [g | u] in bf16. This kernel forms
+//     h = bf16( bf16(silu(g)) * u )          (inference/ops.py:190-192: the
+//                                             reference's F.silu on bf16 and
+//                                             the bf16 product)
+// and stores it in the down GEMM's activation format: one fp32 scale per row
+// and two e4m3 terms, h ~= (hi + lo) * scale. One warp per row, two passes
+// (row amax, then the split; the second pass re-reads g and u from L1/L2).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace dsmoe {
+
+namespace sq {
+__device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
+
+// h = bf16(bf16(silu(g)) * u) for 8 consecutive columns.
+__device__ __forceinline__ void swiglu8(const __nv_bfloat16* g, const __nv_bfloat16* u, float* h) {
+  const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g));
+  const uint4 uv = __ldg(reinterpret_cast<const uint4*>(u));
+  const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv);
+  const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uv);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    h[i] = bf16_round(bf16_round(silu_f32(__bfloat162float(gb[i]))) * __bfloat162float(ub[i]));
+}
+
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ gu, int F,
+                                                           const int32_t* __restrict__ row_end, int P,
+                                                           uint8_t* __restrict__ hq, float* __restrict__ hs) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= *row_end) return;
+  const __nv_bfloat16* g_row = gu + static_cast<size_t>(row) * 2 * F;
+  const __nv_bfloat16* u_row = g_row + F;
+  uint8_t* hi_row = hq + static_cast<size_t>(row) * F;
+  uint8_t* lo_row = hq + (static_cast<size_t>(P) + row) * F;
+  float amax = 0.f;
+  for (int col = lane * 8; col < F; col += 256) {
+    float h[8];
+    swiglu8(g_row + col, u_row + col, h);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(h[i]));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float inv = amax > 0.f ? 448.f / amax : 0.f;
+  if (lane == 0) hs[row] = amax / 448.f;
+  for (int col = lane * 8; col < F; col += 256) {
+    float h[8];
+    swiglu8(g_row + col, u_row + col, h);
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const float q0 = h[i] * inv, q1 = h[i + 1] * inv;
+      const uint16_t h2 = f32x2_to_e4m3x2(q0, q1);
+      const uint16_t l2 = f32x2_to_e4m3x2(q0 - e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff)),
+                                          q1 - e4m3_to_f32(static_cast<uint8_t>(h2 >> 8)));
+      if ((i & 2) == 0) {
+        hw[i >> 2] = h2;
+        lw[i >> 2] = l2;
+      } else {
+        hw[i >> 2] |= static_cast<uint32_t>(h2) << 16;
+        lw[i >> 2] |= static_cast<uint32_t>(l2) << 16;
+      }
+    }
+    *reinterpret_cast<uint2*>(hi_row + col) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(lo_row + col) = make_uint2(lw[0], lw[1]);
+  }
+}
+}  // namespace sq
+
+cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_end, int P, uint8_t* hq,
+                                float* hs, cudaStream_t stream) {
+  if (P == 0) return cudaSuccess;
+  const int blocks = (P * 32 + 255) / 256;
+  sq::swiglu_quant_kernel<<<blocks, 256, 0, stream>>>(gu, F, row_end, P, hq, hs);
+  return cudaGetLastError();
+}
+
+}  // namespace dsmoe

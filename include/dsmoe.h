@@ -145,8 +145,8 @@ DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_feature
  * hooks). Registers up to 8 cudaEvent_t handles that the calling thread's
  * later dsmoe_moe_forward / dsmoe_moe_experts calls record on their stream at
  * stage boundaries: [0] before the router, [1] after it, [2] after the
- * permute, [3] after the gate/up GEMM, [4] after the down GEMM, [5] after the
- * combine. n = 0 switches it off.
+ * permute, [3] after the gate/up GEMM, [4] after the SwiGLU/hi-lo split,
+ * [5] after the down GEMM, [6] after the combine. n = 0 switches it off.
  */
 DSMOE_API int dsmoe_set_profile_events(void* const* events, int32_t n);
 

@@ -44,6 +44,8 @@ def test_version_and_workspace():
     # activations (hi/lo) + h (hi/lo) + y for 9 rows per token dominate
     assert s4096 > 4096 * 9 * (2 * 7168 + 2 * 2048 + 2 * 7168)
     assert L.dsmoe_workspace_size(cfg(hidden=100), 8) == 0
+    for g in (1, 2, 3, 8):  # every multiple of 32 experts plans without error
+        assert L.dsmoe_workspace_size(cfg(n_group=g, n_routed=32 * g, topk_group=1), 4096) > 0
     assert L.dsmoe_expert_ffn_workspace_size(64, 7168, 2048) > 64 * 2 * 7168
     assert L.dsmoe_fp8_linear_workspace_size(64, 7168, 2048) > 64 * 2 * 7168
 

@@ -70,6 +70,17 @@ def test_route_sizes_full_dims(T):
     assert idx.dtype == torch.int64 and w.dtype == torch.float32
 
 
+@pytest.mark.parametrize("n_group,topk_group", [(1, 1), (2, 1), (3, 2)])
+def test_route_other_expert_counts(n_group, topk_group):
+    E = 32 * n_group
+    L = SyntheticLayer(13, 3, 1024, 256, E)
+    x = activations(13, 200, 1024)
+    cfg = cfg_for(1024, 256, E=E, n_group=n_group, topk_group=topk_group)
+    idx, w = ops.route(x.to(DEV), L.gate.to(DEV), cfg)
+    idx_r, w_r = O.route_ref(x, L.gate, n_group, topk_group)
+    assert_routing(idx, w, idx_r, w_r, torch.sigmoid(O.router_logits(x, L.gate)))
+
+
 @pytest.mark.parametrize("T,zipf", [(64, None), (1024, 1.1)])
 def test_route_v3(T, zipf):
     L = SyntheticLayer(3, 3, 7168, 2048, 256, bias_zipf=zipf)
