@@ -109,7 +109,7 @@ Ws plan_moe(int T, int H, int F, int E, int K) {
   const long long pairs = static_cast<long long>(T) * K;
   const long long pad = 31LL * (pairs < E ? pairs : E);
   w.P = round32(T) + round32(static_cast<int>(pairs + pad));
-  w.ksplit = router_ksplit(T, H, E, 148);
+  w.ksplit = router_tc_ksplit(T, H, 148);
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes); return at; };
   w.status = take(sizeof(int));
@@ -187,8 +187,17 @@ int do_route(const dsmoe_moe_config_t* c, const void* hidden, const void* gate, 
   if (!aligned16(hidden) || !aligned16(gate)) return fail(DSMOE_ERR_INVALID, "hidden / gate_weight not 16-byte aligned");
   if (c->router_mode == DSMOE_ROUTER_V3 && !bias) return fail(DSMOE_ERR_INVALID, "router v3 needs score_bias");
   float* partial = at<float>(ws, L.partial);
+  CUtensorMap m_x, m_g;
+  int r;
+  if ((r = make_map(&m_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, c->hidden, T, 64, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B)))
+    return r;
+  if ((r = make_map(&m_g, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gate, c->hidden, c->n_routed, 64, c->n_routed,
+                    CU_TENSOR_MAP_SWIZZLE_128B)))
+    return r;
   prof(0, s);
-  DSMOE_CUDA(launch_router_logits(hidden, gate, partial, T, c->hidden, c->n_routed, L.ksplit, s));
+  DSMOE_CUDA(launch_router_logits_tc(m_x, m_g, partial, T, c->hidden, c->n_routed, L.ksplit, at<int>(ws, L.status),
+                                     s));
   DSMOE_CUDA(launch_router_select(partial, L.ksplit, bias, T, c->n_routed, c->n_group, c->topk_group, c->top_k,
                                   c->router_mode, c->norm_topk_prob, c->routed_scaling_factor, at<int32_t>(ws, L.idx),
                                   idx64, at<float>(ws, L.w), s));

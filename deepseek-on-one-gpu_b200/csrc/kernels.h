@@ -42,10 +42,10 @@ cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, co
 cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_end, int P, uint8_t* hq,
                                 float* hs, cudaStream_t stream);
 
-// Router (router.cu)
-int router_ksplit(int T, int H, int E, int num_sms);
-cudaError_t launch_router_logits(const void* x, const void* gate, float* partial, int T, int H, int E, int ksplit,
-                                 cudaStream_t stream);
+// Router (router_tc.cu logits, router.cu selection)
+int router_tc_ksplit(int T, int H, int num_sms);
+cudaError_t launch_router_logits_tc(const CUtensorMap& tm_x, const CUtensorMap& tm_g, float* partial, int T, int H,
+                                    int E, int ksplit, int* status, cudaStream_t stream);
 cudaError_t launch_router_select(const float* partial, int ksplit, const float* bias, int T, int E, int n_group,
                                  int topk_group, int top_k, int mode, int norm, float scaling, int32_t* idx,
                                  int64_t* idx64, float* w, cudaStream_t stream);

@@ -11,10 +11,8 @@
 // group score = sum of the two largest keys, masked groups -> -inf, weights =
 // unbiased s at the chosen experts / their sum * routed_scaling_factor.
 //
-// Logits: a split-K fp32 SIMT GEMM writes ksplit partial sums; the selection
-// kernel adds them in a fixed order, so results are deterministic. Products of
-// two bf16 values are exact in fp32, so the only difference from the
-// reference's CPU matmul is the order of the fp32 additions.
+// Logits come from router_tc.cu as ksplit partial sums; the selection kernel
+// below adds them in a fixed order, so results are deterministic.
 #include <math_constants.h>
 
 #include "common.cuh"
@@ -23,65 +21,6 @@
 namespace dsmoe {
 
 namespace rt {
-constexpr int BT = 64;  // tokens per block
-constexpr int BE = 64;  // experts per block
-constexpr int BKR = 32;  // k per smem tile
-
-__global__ void __launch_bounds__(256) logits_kernel(const __nv_bfloat16* __restrict__ x,
-                                                     const __nv_bfloat16* __restrict__ gw,
-                                                     float* __restrict__ partial, int T, int H, int E,
-                                                     int k_per_split) {
-  __shared__ __align__(16) float xs[BKR][BT + 4];
-  __shared__ __align__(16) float gs[BKR][BE + 4];
-  const int t0 = blockIdx.x * BT;
-  const int e0 = blockIdx.y * BE;
-  const int ks = blockIdx.z;
-  const int kbeg = ks * k_per_split;
-  const int kend = min(H, kbeg + k_per_split);
-  const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  const int lr = tid >> 2, lk = (tid & 3) * 8;
-  float acc[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-
-  for (int k0 = kbeg; k0 < kend; k0 += BKR) {
-    uint4 xv = make_uint4(0, 0, 0, 0);
-    if (t0 + lr < T) xv = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + lr) * H + k0 + lk));
-    uint4 gv = make_uint4(0, 0, 0, 0);
-    if (e0 + lr < E) gv = __ldg(reinterpret_cast<const uint4*>(gw + static_cast<size_t>(e0 + lr) * H + k0 + lk));
-    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
-    const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv);
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      xs[lk + i][lr] = __bfloat162float(xb[i]);
-      gs[lk + i][lr] = __bfloat162float(gb[i]);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < BKR; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&xs[kk][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&gs[kk][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w};
-      const float bv[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + ty * 4 + i;
-    if (t < T && e0 + tx * 4 < E)
-      *reinterpret_cast<float4*>(partial + (static_cast<size_t>(ks) * T + t) * E + e0 + tx * 4) =
-          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-  }
-}
-
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -202,27 +141,6 @@ __global__ void __launch_bounds__(256) select_kernel(const float* __restrict__ p
   }
 }
 }  // namespace rt
-
-int router_ksplit(int T, int H, int E, int num_sms) {
-  const int k_tiles = H / rt::BKR;
-  const int base = ((T + rt::BT - 1) / rt::BT) * ((E + rt::BE - 1) / rt::BE);
-  if (base <= 0) return 1;
-  int want = (2 * num_sms + base - 1) / base;
-  if (want < 1) want = 1;
-  int best = 1;
-  for (int d = 1; d <= k_tiles && d <= 64; ++d)
-    if (k_tiles % d == 0 && d <= want) best = d;
-  return best;
-}
-
-cudaError_t launch_router_logits(const void* x, const void* gate, float* partial, int T, int H, int E, int ksplit,
-                                 cudaStream_t stream) {
-  const int kps = (H / rt::BKR / ksplit) * rt::BKR;
-  dim3 grid((T + rt::BT - 1) / rt::BT, (E + rt::BE - 1) / rt::BE, ksplit);
-  rt::logits_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
-                                              static_cast<const __nv_bfloat16*>(gate), partial, T, H, E, kps);
-  return cudaGetLastError();
-}
 
 cudaError_t launch_router_select(const float* partial, int ksplit, const float* bias, int T, int E, int n_group,
                                  int topk_group, int top_k, int mode, int norm, float scaling, int32_t* idx,
