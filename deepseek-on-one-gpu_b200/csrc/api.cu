@@ -98,7 +98,7 @@ int num_sms() {
 struct Ws {
   size_t status = 0, counts = 0, cursor = 0, row_start = 0, us_up = 0, us_dn = 0, slot0 = 0;
   size_t partial = 0, idx = 0, w = 0, pos = 0, xq = 0, sx = 0, gu = 0, hq = 0, hs = 0, y = 0, total = 0;
-  int P = 0, ksplit = 1, NG = 1;
+  int P = 0, ksplit = 1, NG = 1, tile = 32;
 };
 
 // Routed MoE block: groups = shared + n_routed; rows = shared segment +
@@ -110,6 +110,7 @@ Ws plan_moe(int T, int H, int F, int E, int K) {
   const long long pad = 31LL * (pairs < E ? pairs : E);
   w.P = round32(T) + round32(static_cast<int>(pairs + pad));
   w.ksplit = router_tc_ksplit(T, H, 148);
+  w.tile = gemm_tile_tokens(T);
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes); return at; };
   w.status = take(sizeof(int));
@@ -138,6 +139,7 @@ Ws plan_single(int T, int K_in, int F /* 0 for a plain linear */) {
   Ws w;
   w.NG = 1;
   w.P = round32(T);
+  w.tile = gemm_tile_tokens(T);
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes); return at; };
   w.status = take(sizeof(int));
@@ -231,6 +233,7 @@ struct GemmJob {
   int P;
   const int32_t *counts, *row_start, *unit_start, *slot_of;
   int n_groups;
+  int tile;             // token tile (gemm_tile_tokens)
   __nv_bfloat16* y;     // [P][n_mat * M]
   int* status;
 };
@@ -243,7 +246,7 @@ int run_gemm(const GemmJob& j, cudaStream_t s) {
     return r;
   if ((r = make_map(&m_w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.w1, j.K, rows, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
     return r;
-  if ((r = make_map(&m_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.xq, j.K, 2ull * j.P, 128, GEMM_BN,
+  if ((r = make_map(&m_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.xq, j.K, 2ull * j.P, 128, j.tile,
                     CU_TENSOR_MAP_SWIZZLE_128B)))
     return r;
   if ((r = make_map(&m_x32, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, j.xq, j.K, 2ull * j.P, 128, 32,
@@ -265,7 +268,7 @@ int run_gemm(const GemmJob& j, cudaStream_t s) {
   gp.sx = j.sx;
   gp.y = j.y;
   gp.status = j.status;
-  DSMOE_CUDA(launch_grouped_gemm(m_w0, m_w1, m_x, m_x32, gp, num_sms(), s));
+  DSMOE_CUDA(launch_grouped_gemm(m_w0, m_w1, m_x, m_x32, gp, j.tile, num_sms(), s));
   return DSMOE_OK;
 }
 
@@ -280,6 +283,7 @@ int run_ffn(const void* w_gate, const float* s_gate, const void* w_up, const flo
   j.row_start = at<int32_t>(ws, L.row_start);
   j.slot_of = slot_of;
   j.n_groups = n_groups;
+  j.tile = L.tile;
   j.status = at<int>(ws, L.status);
   int r;
   j.w0 = w_gate;
@@ -326,7 +330,7 @@ int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, con
   int32_t* pos = at<int32_t>(ws, L.pos);
 
   DSMOE_CUDA(launch_count(idx, T * K, counts, NG, s));
-  DSMOE_CUDA(launch_plan(counts, NG, T, 2 * F / 128, H / 128, row_start, cursor, us_up, us_dn, s));
+  DSMOE_CUDA(launch_plan(counts, NG, T, L.tile, 2 * F / 128, H / 128, row_start, cursor, us_up, us_dn, s));
   DSMOE_CUDA(launch_quant_scatter(hidden, T, H, idx, K, 1, row_start, cursor, L.P, at<uint8_t>(ws, L.xq),
                                   at<float>(ws, L.sx), pos, s));
   prof(2, s);
@@ -427,7 +431,7 @@ size_t dsmoe_fp8_linear_workspace_size(int32_t tokens, int32_t in_features, int3
 static int single_prologue(const void* x, int T, int K_in, int mt_up, int mt_dn, const Ws& L, void* ws,
                            cudaStream_t s) {
   DSMOE_CUDA(cudaMemsetAsync(at<int32_t>(ws, L.slot0), 0, 4, s));
-  DSMOE_CUDA(launch_plan(at<int32_t>(ws, L.counts), 1, T, mt_up, mt_dn, at<int32_t>(ws, L.row_start),
+  DSMOE_CUDA(launch_plan(at<int32_t>(ws, L.counts), 1, T, L.tile, mt_up, mt_dn, at<int32_t>(ws, L.row_start),
                          at<int32_t>(ws, L.cursor), at<int32_t>(ws, L.us_up), at<int32_t>(ws, L.us_dn), s));
   DSMOE_CUDA(launch_quant_scatter(x, T, K_in, nullptr, 0, 1, at<int32_t>(ws, L.row_start),
                                   at<int32_t>(ws, L.cursor), L.P, at<uint8_t>(ws, L.xq), at<float>(ws, L.sx), nullptr,
@@ -490,6 +494,7 @@ int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_features, int32_t
   j.unit_start = at<int32_t>(workspace, L.us_dn);
   j.slot_of = at<int32_t>(workspace, L.slot0);
   j.n_groups = 1;
+  j.tile = L.tile;
   j.y = static_cast<__nv_bfloat16*>(out);
   j.status = at<int>(workspace, L.status);
   return run_gemm(j, s);

@@ -9,10 +9,11 @@
 // share one fp32 scale per row: x ~= (hi + lo) * sx[r].
 //
 // Mapping to the tensor core ("swap AB"): the weight tile is the 128-row A
-// operand (M = 128 output features), the tokens are the N operand (N = 16..BN
-// tokens, a multiple of 16), so decode-sized groups of a few tokens waste
-// little work. For every 128-wide K block the MMA writes a fresh fp32 partial
-// (hi and lo accumulate into the same partial) into one of two TMEM buffers;
+// operand (M = 128 output features), the tokens are the N operand, so
+// decode-sized groups of a few tokens waste little work. For every 128-wide K
+// block the MMA writes a fresh fp32 partial of W*hi + W*lo into one of NBUF
+// TMEM buffers (tiles of up to 128 tokens put hi and lo side by side in one
+// MMA of N = 2 * tile; wider tiles accumulate hi then lo along K);
 // the epilogue warps read it back and promote it with the block's weight scale:
 //     acc[m, r] += sw[mb, kb] * partial[m, r]
 // and finally write bf16(acc * sx[r]) — the reference's fp32
@@ -48,22 +49,30 @@ constexpr int NUM_EPI_WARPS = 16;
 constexpr int NUM_THREADS = (2 + NUM_EPI_WARPS) * 32;
 constexpr int MAX_GROUPS = 264;
 
-template <int BN_, int STAGES_>
+template <int BN_, int STAGES_, int NBUF_>
 struct Cfg {
   static constexpr int BN = BN_;                  // max tokens per tile
   static constexpr int STAGES = STAGES_;
+  static constexpr int NBUF = NBUF_;              // TMEM accumulator buffers (MMA runs NBUF-1 K steps ahead)
+  // hi and lo rows are adjacent in shared memory; for tiles of up to 128
+  // tokens one MMA covers both (N = 2 * BN, columns [0,BN) hi, [BN,2BN) lo),
+  // halving the MMA count; wider tiles accumulate hi then lo along K.
+  static constexpr bool NCAT = 2 * BN <= 256;
+  static constexpr int TCOLS = NCAT ? 2 * BN : BN;  // TMEM columns per buffer
   static constexpr int EPI_COLS = BN / 4;         // accumulator columns per epilogue warp
+  static constexpr int CHUNK = EPI_COLS < 16 ? EPI_COLS : 16;  // columns per TMEM load
   static constexpr int XH_OFF = BM * BK;
   static constexpr int XL_OFF = XH_OFF + BN * BK;
   static constexpr int STAGE_BYTES = XL_OFF + BN * BK;  // multiple of 1024 for BN % 8 == 0
-  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = NBUF * TCOLS <= 32 ? 32 : NBUF * TCOLS <= 64 ? 64 : NBUF * TCOLS <= 128 ? 128
+                                   : NBUF * TCOLS <= 256 ? 256 : 512;
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-  // barriers: full[S], empty[S], tfull[2], tempty[2], done
-  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  // barriers: full[S], empty[S], tfull[NBUF], tempty[NBUF], done
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * NBUF + 1;
   static constexpr int MISC_OFF = BAR_OFF + 8 * NUM_BARS;
   static constexpr int TABLE_OFF = ((MISC_OFF + 16 + 15) / 16) * 16;
   static constexpr int SMEM_BYTES = TABLE_OFF + 4 * 4 * MAX_GROUPS + 1024;  // + alignment slack
-  static_assert(BN % 16 == 0 && BN <= 256 && EPI_COLS % 16 == 0, "tile shape");
+  static_assert(BN % 32 == 0 && BN <= 256 && EPI_COLS % CHUNK == 0 && NBUF * TCOLS <= 512, "tile shape");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
@@ -84,22 +93,24 @@ __device__ __forceinline__ void decode_unit(int u, int n_groups, const int* usta
   nt = local - mt * ntiles;
 }
 
-template <int BN_, int STAGES_>
+template <int BN_, int STAGES_, int NBUF_>
 __global__ void __maxnreg__(96)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_x32,
                     const GemmParams p) {
-  using C = Cfg<BN_, STAGES_>;
+  using C = Cfg<BN_, STAGES_, NBUF_>;
   constexpr int BN = C::BN;
   constexpr int STAGES = C::STAGES;
+  constexpr int NBUF = C::NBUF;
   constexpr int EPI_COLS = C::EPI_COLS;
+  constexpr int CHUNK = C::CHUNK;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* done_bar = tempty + 2;
+  uint64_t* tempty = tfull + NBUF;
+  uint64_t* done_bar = tempty + NBUF;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
   int* s_ustart = reinterpret_cast<int*>(smem + C::TABLE_OFF);
@@ -124,7 +135,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], NUM_EPI_WARPS);
     }
@@ -171,7 +182,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         const int col0 = nt * BN;
         const int ncols = min(BN, s_counts[g] - col0);
         const int nsub = (ncols + SUB - 1) / SUB;
-        const bool small = nsub * SUB < BN && nsub <= 2;  // a few 32-row boxes beat one BN-row box
+        const bool small = BN == SUB || (nsub * SUB < BN && nsub <= 2);  // a few 32-row boxes beat one big box
         const int row0 = s_rows[g] + col0;
         const int wrow = slot * p.M + (mt - mat * mt_per_mat) * BM;
         const uint32_t bytes = BM * BK + 2 * (small ? nsub * SUB : BN) * BK;
@@ -214,27 +225,33 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         int g, mt, nt;
         decode_unit<BN>(u, NG, s_ustart, s_counts, g, mt, nt);
         const int ncols = min(BN, s_counts[g] - nt * BN);
-        const int N = (ncols + 15) & ~15;
+        const int N = C::NCAT ? 2 * BN : (ncols + 15) & ~15;
         const uint32_t idesc = idesc_e4m3(BM, N);
         for (int kb = 0; kb < n_kb; ++kb) {
           if (!mbar_wait(&tempty[tb], tphase ^ 1, p.status, kDevTimeoutMma, s_abort)) { ok = false; break; }
           if (!mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma, s_abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sbase = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t d = tmem_base + tb * C::TCOLS;
+          if constexpr (C::NCAT) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t xoff = h ? C::XL_OFF : C::XH_OFF;
+            for (int kk = 0; kk < BK / 32; ++kk)
+              mma_f8f6f4(d, umma_desc_sw128(sbase + kk * 32), umma_desc_sw128(sbase + C::XH_OFF + kk * 32), idesc,
+                         kk != 0);
+          } else {
 #pragma unroll
-            for (int kk = 0; kk < BK / 32; ++kk) {
-              mma_f8f6f4(tmem_base + tb * BN, umma_desc_sw128(sbase + kk * 32),
-                         umma_desc_sw128(sbase + xoff + kk * 32), idesc, (h | kk) != 0);
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t xoff = h ? C::XL_OFF : C::XH_OFF;
+#pragma unroll
+              for (int kk = 0; kk < BK / 32; ++kk)
+                mma_f8f6f4(d, umma_desc_sw128(sbase + kk * 32), umma_desc_sw128(sbase + xoff + kk * 32), idesc,
+                           (h | kk) != 0);
             }
           }
           mma_commit(&empty[stage]);
           mma_commit(&tfull[tb]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
-          tb ^= 1;
-          if (tb == 0) tphase ^= 1;
+          if (++tb == NBUF) { tb = 0; tphase ^= 1; }
         }
       }
       // All MMAs issued by this thread complete before TMEM is released.
@@ -278,20 +295,30 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         tc_fence_after();
         const float sw = __shfl_sync(0xffffffffu, kb < 32 ? swr0 : swr1, kb & 31);
 #pragma unroll
-        for (int q = 0; q < EPI_COLS / 16; ++q) {
-          if (q * 16 < nvalid) {  // warp-uniform
-            float part[16];
-            tmem_ld16(tmem_base + lane_base + tb * BN + c0 + q * 16, part);
-            tmem_ld_wait();
+        for (int q = 0; q < EPI_COLS / CHUNK; ++q) {
+          if (q * CHUNK < nvalid) {  // warp-uniform
+            const uint32_t ta = tmem_base + lane_base + tb * C::TCOLS + c0 + q * CHUNK;
+            float part[CHUNK];
+            if constexpr (CHUNK == 16) tmem_ld16(ta, part);
+            else tmem_ld8(ta, part);
+            if constexpr (C::NCAT) {
+              float lo[CHUNK];
+              if constexpr (CHUNK == 16) tmem_ld16(ta + BN, lo);
+              else tmem_ld8(ta + BN, lo);
+              tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[q * 16 + i] = fmaf(part[i], sw, acc[q * 16 + i]);
+              for (int i = 0; i < CHUNK; ++i) part[i] += lo[i];
+            } else {
+              tmem_ld_wait();
+            }
+#pragma unroll
+            for (int i = 0; i < CHUNK; ++i) acc[q * CHUNK + i] = fmaf(part[i], sw, acc[q * CHUNK + i]);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[tb]);
-        tb ^= 1;
-        if (tb == 0) tphase ^= 1;
+        if (++tb == NBUF) { tb = 0; tphase ^= 1; }
       }
       if (!ok) break;
       const int row_base = s_rows[g] + nt * BN + c0;
@@ -314,33 +341,46 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int NBUF>
 cudaError_t launch_cfg(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const CUtensorMap& x32,
                        const GemmParams& p, int grid, cudaStream_t stream) {
-  using C = Cfg<BN, STAGES>;
+  using C = Cfg<BN, STAGES, NBUF>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, NBUF>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  grouped_gemm_kernel<BN, STAGES><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(w0, w1, x, x32, p);
+  grouped_gemm_kernel<BN, STAGES, NBUF><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(w0, w1, x, x32, p);
   return cudaGetLastError();
 }
 
 }  // namespace gg
 
-int gemm_tile_tokens() { return GEMM_BN; }
+// Token tile for a launch over `tokens` tokens: no group can hold more than
+// `tokens` rows, so small batches get narrow tiles and many TMEM buffers.
+int gemm_tile_tokens(int tokens) {
+  if (tokens <= 32) return 32;
+  if (tokens <= 64) return 64;
+  if (tokens <= 128) return 128;
+  return 192;
+}
 
 cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
-                                const CUtensorMap& x32, const GemmParams& p, int grid, cudaStream_t stream) {
+                                const CUtensorMap& x32, const GemmParams& p, int tile, int grid, cudaStream_t stream) {
   if (p.n_groups > gg::MAX_GROUPS - 1 || p.K / gg::BK > 64 || (p.n_mat != 1 && p.n_mat != 2))
     return cudaErrorInvalidValue;
-  return gg::launch_cfg<GEMM_BN, GEMM_STAGES>(w0, w1, x, x32, p, grid, stream);
+  switch (tile) {
+    case 32: return gg::launch_cfg<32, 8, 8>(w0, w1, x, x32, p, grid, stream);
+    case 64: return gg::launch_cfg<64, 6, 4>(w0, w1, x, x32, p, grid, stream);
+    case 128: return gg::launch_cfg<128, 4, 2>(w0, w1, x, x32, p, grid, stream);
+    case 192: return gg::launch_cfg<192, 3, 2>(w0, w1, x, x32, p, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace dsmoe

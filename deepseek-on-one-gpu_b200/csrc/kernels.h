@@ -8,11 +8,6 @@
 
 namespace dsmoe {
 
-// Token tile of the grouped GEMM (max tokens per work unit) and its pipeline
-// depth; the unit plan (permute.cu) counts tiles of the same size.
-constexpr int GEMM_BN = 192;
-constexpr int GEMM_STAGES = 3;
-
 // Group-table convention used by every kernel: group 0 is the shared expert
 // (every token, in token order), group 1 + e is routed expert e.
 struct GemmParams {
@@ -33,10 +28,12 @@ struct GemmParams {
   int* status;          // device error word
 };
 
-int gemm_tile_tokens();
-// x: activation map with GEMM_BN-row boxes, x32: the same rows with 32-row boxes.
+// Token tile (max tokens per work unit) of the grouped GEMM for a launch over
+// `tokens` tokens; the unit plan (permute.cu) must count tiles of this size.
+int gemm_tile_tokens(int tokens);
+// x: activation map with `tile`-row boxes, x32: the same rows with 32-row boxes.
 cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
-                                const CUtensorMap& x32, const GemmParams& p, int grid, cudaStream_t stream);
+                                const CUtensorMap& x32, const GemmParams& p, int tile, int grid, cudaStream_t stream);
 
 // SwiGLU + hi/lo split (swiglu_quant.cu)
 cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_end, int P, uint8_t* hq,
@@ -52,8 +49,9 @@ cudaError_t launch_router_select(const float* partial, int ksplit, const float* 
 
 // Permutation (permute.cu)
 cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream);
-cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int mt_up, int mt_dn, int32_t* row_start,
-                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, cudaStream_t stream);
+cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int tile, int mt_up, int mt_dn,
+                        int32_t* row_start, int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn,
+                        cudaStream_t stream);
 cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int has_shared,
                                  const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq, float* sx,
                                  int32_t* pos, cudaStream_t stream);

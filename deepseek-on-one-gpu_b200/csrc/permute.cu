@@ -56,7 +56,7 @@ __device__ __forceinline__ int block_excl_scan(int v, int* buf) {
 }
 
 __global__ void __launch_bounds__(MAX_GROUPS) plan_kernel(int32_t* __restrict__ counts, int n_groups,
-                                                          int shared_tokens, int mt_up, int mt_dn,
+                                                          int shared_tokens, int tile, int mt_up, int mt_dn,
                                                           int32_t* __restrict__ row_start,
                                                           int32_t* __restrict__ cursor,
                                                           int32_t* __restrict__ ustart_up,
@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(MAX_GROUPS) plan_kernel(int32_t* __restrict__ 
   if (i < n_groups) c = i == 0 ? shared_tokens : counts[i];
   __syncthreads();
   if (i == 0) counts[0] = shared_tokens;
-  const int nt = (c + GEMM_BN - 1) / GEMM_BN;
+  const int nt = (c + tile - 1) / tile;
   const int seg = block_excl_scan<MAX_GROUPS>((c + 31) & ~31, buf);
   const int uu = block_excl_scan<MAX_GROUPS>(mt_up * nt, buf);
   const int ud = block_excl_scan<MAX_GROUPS>(mt_dn * nt, buf);
@@ -167,11 +167,12 @@ cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n
   return cudaGetLastError();
 }
 
-cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int mt_up, int mt_dn, int32_t* row_start,
-                        int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn, cudaStream_t stream) {
+cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int tile, int mt_up, int mt_dn,
+                        int32_t* row_start, int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn,
+                        cudaStream_t stream) {
   if (n_groups + 1 > pm::MAX_GROUPS) return cudaErrorInvalidValue;
-  pm::plan_kernel<<<1, pm::MAX_GROUPS, 0, stream>>>(counts, n_groups, shared_tokens, mt_up, mt_dn, row_start, cursor,
-                                                    ustart_up, ustart_dn);
+  pm::plan_kernel<<<1, pm::MAX_GROUPS, 0, stream>>>(counts, n_groups, shared_tokens, tile, mt_up, mt_dn, row_start,
+                                                    cursor, ustart_up, ustart_dn);
   return cudaGetLastError();
 }
 
