@@ -236,6 +236,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+
 // --------------------------------------------------------------- numerics
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));

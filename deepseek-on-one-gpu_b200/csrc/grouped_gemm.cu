@@ -49,7 +49,7 @@ constexpr int NUM_EPI_WARPS = 16;
 constexpr int NUM_THREADS = (2 + NUM_EPI_WARPS) * 32;
 constexpr int MAX_GROUPS = 264;
 
-template <int BN_, int STAGES_, int NBUF_>
+template <int BN_, int STAGES_, int NBUF_, bool NCAT_>
 struct Cfg {
   static constexpr int BN = BN_;                  // max tokens per tile
   static constexpr int STAGES = STAGES_;
@@ -57,10 +57,10 @@ struct Cfg {
   // hi and lo rows are adjacent in shared memory; for tiles of up to 128
   // tokens one MMA covers both (N = 2 * BN, columns [0,BN) hi, [BN,2BN) lo),
   // halving the MMA count; wider tiles accumulate hi then lo along K.
-  static constexpr bool NCAT = 2 * BN <= 256;
+  static constexpr bool NCAT = NCAT_;
   static constexpr int TCOLS = NCAT ? 2 * BN : BN;  // TMEM columns per buffer
   static constexpr int EPI_COLS = BN / 4;         // accumulator columns per epilogue warp
-  static constexpr int CHUNK = EPI_COLS < 16 ? EPI_COLS : 16;  // columns per TMEM load
+  static constexpr int CHUNK = EPI_COLS % 16 ? 8 : 16;  // columns per TMEM load
   static constexpr int XH_OFF = BM * BK;
   static constexpr int XL_OFF = XH_OFF + BN * BK;
   static constexpr int STAGE_BYTES = XL_OFF + BN * BK;  // multiple of 1024 for BN % 8 == 0
@@ -72,7 +72,8 @@ struct Cfg {
   static constexpr int MISC_OFF = BAR_OFF + 8 * NUM_BARS;
   static constexpr int TABLE_OFF = ((MISC_OFF + 16 + 15) / 16) * 16;
   static constexpr int SMEM_BYTES = TABLE_OFF + 4 * 4 * MAX_GROUPS + 1024;  // + alignment slack
-  static_assert(BN % 32 == 0 && BN <= 256 && EPI_COLS % CHUNK == 0 && NBUF * TCOLS <= 512, "tile shape");
+  static_assert(BN % 32 == 0 && BN <= 256 && EPI_COLS % CHUNK == 0 && NBUF * TCOLS <= 512 &&
+                    (!NCAT || 2 * BN <= 256), "tile shape");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
@@ -93,12 +94,12 @@ __device__ __forceinline__ void decode_unit(int u, int n_groups, const int* usta
   nt = local - mt * ntiles;
 }
 
-template <int BN_, int STAGES_, int NBUF_>
+template <int BN_, int STAGES_, int NBUF_, bool NCAT_>
 __global__ void __maxnreg__(96)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_x32,
                     const GemmParams p) {
-  using C = Cfg<BN_, STAGES_, NBUF_>;
+  using C = Cfg<BN_, STAGES_, NBUF_, NCAT_>;
   constexpr int BN = C::BN;
   constexpr int STAGES = C::STAGES;
   constexpr int NBUF = C::NBUF;
@@ -341,21 +342,21 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
-template <int BN, int STAGES, int NBUF>
+template <int BN, int STAGES, int NBUF, bool NCAT>
 cudaError_t launch_cfg(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const CUtensorMap& x32,
                        const GemmParams& p, int grid, cudaStream_t stream) {
-  using C = Cfg<BN, STAGES, NBUF>;
+  using C = Cfg<BN, STAGES, NBUF, NCAT>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, NBUF>,
+    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, NBUF, NCAT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  grouped_gemm_kernel<BN, STAGES, NBUF><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(w0, w1, x, x32, p);
+  grouped_gemm_kernel<BN, STAGES, NBUF, NCAT><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(w0, w1, x, x32, p);
   return cudaGetLastError();
 }
 
@@ -367,7 +368,7 @@ int gemm_tile_tokens(int tokens) {
   if (tokens <= 32) return 32;
   if (tokens <= 64) return 64;
   if (tokens <= 128) return 128;
-  return 192;
+  return 160;
 }
 
 cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
@@ -375,10 +376,10 @@ cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, co
   if (p.n_groups > gg::MAX_GROUPS - 1 || p.K / gg::BK > 64 || (p.n_mat != 1 && p.n_mat != 2))
     return cudaErrorInvalidValue;
   switch (tile) {
-    case 32: return gg::launch_cfg<32, 8, 8>(w0, w1, x, x32, p, grid, stream);
-    case 64: return gg::launch_cfg<64, 6, 4>(w0, w1, x, x32, p, grid, stream);
-    case 128: return gg::launch_cfg<128, 4, 2>(w0, w1, x, x32, p, grid, stream);
-    case 192: return gg::launch_cfg<192, 3, 2>(w0, w1, x, x32, p, grid, stream);
+    case 32: return gg::launch_cfg<32, 8, 8, true>(w0, w1, x, x32, p, grid, stream);
+    case 64: return gg::launch_cfg<64, 6, 4, true>(w0, w1, x, x32, p, grid, stream);
+    case 128: return gg::launch_cfg<128, 4, 2, true>(w0, w1, x, x32, p, grid, stream);
+    case 160: return gg::launch_cfg<160, 3, 3, false>(w0, w1, x, x32, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
