@@ -348,6 +348,9 @@ int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, con
 }
 
 }  // namespace
+
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 }  // namespace dsmoe
 
 using namespace dsmoe;

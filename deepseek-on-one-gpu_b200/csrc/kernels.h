@@ -8,6 +8,9 @@
 
 namespace dsmoe {
 
+// Records `msg` as the calling thread's dsmoe_last_error() and returns `code`.
+int set_last_error(int code, const char* msg);
+
 // Group-table convention used by every kernel: group 0 is the shared expert
 // (every token, in token order), group 1 + e is routed expert e.
 struct GemmParams {

@@ -22,6 +22,7 @@ EXPORTED = (
     "dsmoe_last_error", "dsmoe_version", "dsmoe_workspace_size", "dsmoe_route", "dsmoe_moe_forward",
     "dsmoe_moe_experts", "dsmoe_expert_ffn_workspace_size", "dsmoe_fp8_linear_workspace_size",
     "dsmoe_expert_ffn", "dsmoe_fp8_linear", "dsmoe_read_status", "dsmoe_set_profile_events",
+    "dsmoe_expert_ffn_noalloc",
 )
 
 
@@ -74,6 +75,7 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_fp8_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, sz, vp]
                 L.dsmoe_read_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
                 L.dsmoe_set_profile_events.argtypes = [ctypes.POINTER(vp), i32]
+                L.dsmoe_expert_ffn_noalloc.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]
                 for name in EXPORTED:
                     getattr(L, name).restype = getattr(L, name).restype or ctypes.c_int
                 _lib = L

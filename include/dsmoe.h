@@ -150,6 +150,39 @@ DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_feature
  */
 DSMOE_API int dsmoe_set_profile_events(void* const* events, int32_t n);
 
+/*
+ * Allocation-free variant of dsmoe_expert_ffn (no counterpart in the
+ * reference; an addition of this library).
+ *
+ * Some callers cannot allocate device memory at call time: a runtime that
+ * owns all device memory through its own fixed pool and forbids any other
+ * allocation, code that runs while an allocator lock is held (for instance
+ * from a memory-pressure or allocation callback), and latency-critical paths
+ * that must not take an allocation that can block, synchronize the device or
+ * fail under memory pressure. This entry point computes the same result as
+ * dsmoe_expert_ffn without a workspace argument and without calling cudaMalloc,
+ * cudaFree or any allocating routine: its scratch is a fixed array of
+ * DSMOE_NOALLOC_SCRATCH_BYTES inside the library, one per GPU, held by every
+ * GPU that loads the library until the process exits.
+ *
+ *   - The caller still provides x, the weights and out (same layouts as
+ *     dsmoe_expert_ffn).
+ *   - Shapes whose scratch need (dsmoe_expert_ffn_workspace_size) exceeds
+ *     DSMOE_NOALLOC_SCRATCH_BYTES are rejected with DSMOE_ERR_WORKSPACE before
+ *     any work is enqueued (about 300 tokens at hidden 7168, inter 2048).
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls on a device share the one array, and it keeps the previous
+ *     call's contents (the call clears what must start at zero). Calls whose
+ *     work can overlap on the GPU race on the array: issue them on one stream
+ *     or order them with events.
+ */
+#define DSMOE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+DSMOE_API int dsmoe_expert_ffn_noalloc(const void* x, int32_t tokens, int32_t hidden, int32_t inter,
+                                       const void* w_gate, const float* s_gate, const void* w_up, const float* s_up,
+                                       const void* w_down, const float* s_down, void* out, dsmoe_stream_t stream);
+
 /* Reads (synchronously) and clears the device error word kept in `workspace`. */
 DSMOE_API int dsmoe_read_status(void* workspace, int32_t* device_status, dsmoe_stream_t stream);
 
