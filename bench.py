@@ -40,6 +40,16 @@ UNIT = "tokens/s"
 H, F, E, TOPK = 7168, 2048, 256, 8
 LAYER = 3
 FP8_DENSE_NOMINAL_TFLOPS = 4500.0
+# DRAM bytes (read + write) per gate/up work unit (one 128-row weight tile x
+# one token tile) measured by ncu on a 33-expert, T=512 launch of the same
+# kernel: 1.109 GB over 1,152 units. The full-size launch is too large for a
+# multi-pass ncu capture, so its traffic is this figure times its units.
+GATEUP_DRAM_BYTES_PER_UNIT = 1.109e9 / 1152
+
+
+def gemm_tile(tokens: int) -> int:
+    """Token tile the library picks for a launch over `tokens` tokens."""
+    return 32 if tokens <= 32 else 64 if tokens <= 64 else 128 if tokens <= 128 else 160
 
 
 def peaks():
@@ -256,9 +266,14 @@ def main():
     dominant = "gate_up" if gu_ms >= dn_ms else "down"
     dom_bytes, dom_ms = (gateup_bytes, gu_ms) if dominant == "gate_up" else (down_bytes, dn_ms)
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
+    tile = gemm_tile(T)
+    per_group = [T] + counts.tolist()
+    gateup_units = sum((2 * F // 128) * ((c + tile - 1) // tile) for c in per_group)
+    traffic = GATEUP_DRAM_BYTES_PER_UNIT * gateup_units if dominant == "gate_up" else None
     roofline = {"kernel": f"grouped_gemm_kernel ({dominant})",
                 "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak, "peak_source": peak_src, "traffic": None,
+                "frac": achieved / hbm_peak, "peak_source": peak_src, "traffic": traffic,
+                "traffic_source": "ncu DRAM bytes per work unit of a 33-expert T=512 capture x units of this launch",
                 "algorithmic_bytes_per_launch": dom_bytes}
     layer_bytes = gateup_bytes + swiglu_bytes + down_bytes
     layer_ms = sum(stage_ms)
