@@ -171,7 +171,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="dsmoe", choices=["dsmoe", "reference"])
-    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per GPU (default 4096 on 1 GPU - config 2; 8192 per GPU expert-parallel - config 3)")
+    ap.add_argument("--mode", default="ep", choices=["ep", "replica"],
+                    help="N > 1: expert-parallel over NCCL (default) or independent replicas")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--ref-tokens-per-step", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -184,6 +187,8 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.tokens is None:
+        args.tokens = 4096 if world == 1 else 8192
     if args.impl == "reference":
         run_reference(args, rank)
         return
@@ -203,13 +208,28 @@ def main():
     T = args.tokens
     n_group = max(1, args.experts // 32)
     cfg = DeepSeekConfig(n_routed_experts=32 * n_group, n_group=n_group, topk_group=min(4, n_group))
-    store = SyntheticWeightStore(cfg, seed=1 + rank, device=dev, pin_memory=False, gen_device="cuda")
-    gt = GPUTransfer(cfg, store, dev)
-    bank = gt.bank(LAYER)
-    x = activations(1 + rank, T, H, device=dev)
+    ep = world > 1 and args.mode == "ep"
+    if ep:
+        # config 3: one set of layer weights (seed 2) sharded over the ranks,
+        # every rank with its own 8192 tokens
+        from dsmoe.ep import DistExchange, EPLayer
 
-    def step(inp):
-        return moe_block(inp, LAYER, store, gt, cfg)
+        store = SyntheticWeightStore(cfg, seed=2, device=dev, pin_memory=False, gen_device="cuda")
+        ep_layer = EPLayer(cfg, store, dev, LAYER, world, rank, exchange=DistExchange(),
+                           expert_source=store.device_expert)
+        bank = None
+        x = activations(2000 + rank, T, H, device=dev)
+
+        def step(inp):
+            return ep_layer.forward(inp)
+    else:
+        store = SyntheticWeightStore(cfg, seed=1 + rank, device=dev, pin_memory=False, gen_device="cuda")
+        gt = GPUTransfer(cfg, store, dev)
+        bank = gt.bank(LAYER)
+        x = activations(1 + rank, T, H, device=dev)
+
+        def step(inp):
+            return moe_block(inp, LAYER, store, gt, cfg)
 
     # ---------------------------------------------------------- device-timed
     for _ in range(args.warmup):
@@ -242,17 +262,41 @@ def main():
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
     set_profile_events(evs)
     names = ["router", "permute", "gate_up", "swiglu_quant", "down", "combine"]
+    if ep:
+        names[1] = "dispatch+all_to_all+permute"
     stage_ms = [0.0] * len(names)
     n_prof = max(3, args.steps // 2)
     for _ in range(n_prof):
-        out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)
+        if ep:
+            # stage events come from the route and the rank's expert GEMMs; the
+            # shared-expert FFN in the last phase must not re-record them
+            counts_d, tok_rows, send_x, meta = ep_layer.dispatch(x)
+            sc, rc = ep_layer.exchange.counts(counts_d)
+            recv_meta = ep_layer.exchange.rows(meta, sc, rc)
+            part = ep_layer.compute(ep_layer.exchange.rows(send_x, sc, rc), recv_meta)
+            set_profile_events(None)
+            ep_layer.finish(x, ep_layer.exchange.rows(part, rc, sc), tok_rows)
+            torch.cuda.synchronize()
+            set_profile_events(evs)
+            from dsmoe.ops import route as _route
+            idx, _w = _route(x, store.get_gate_weight(LAYER), cfg)
+        else:
+            out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)
         torch.cuda.synchronize()
         for i in range(len(names)):
             stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
     set_profile_events(None)
-    counts = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).cpu()
-    touched = int((counts > 0).sum()) + 1  # + shared expert
-    rows = T * TOPK + T
+    if ep:
+        # the rank's own GEMM work: its experts over the rows it received (no shared expert there)
+        lidx = recv_meta[:, :TOPK].reshape(-1)
+        lidx = lidx[lidx >= 0].long()
+        counts = torch.bincount(lidx, minlength=ep_layer.El).cpu()
+        touched = int((counts > 0).sum())
+        rows = int(lidx.numel())
+    else:
+        counts = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).cpu()
+        touched = int((counts > 0).sum()) + 1  # + shared expert
+        rows = T * TOPK + T
     w13 = 2 * F * H + 2 * (F // 128) * (H // 128) * 4
     w2 = F * H + (F // 128) * (H // 128) * 4
     # algorithmic bytes per launch: weights of every expert used, activations
@@ -266,8 +310,8 @@ def main():
     dominant = "gate_up" if gu_ms >= dn_ms else "down"
     dom_bytes, dom_ms = (gateup_bytes, gu_ms) if dominant == "gate_up" else (down_bytes, dn_ms)
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
-    tile = gemm_tile(T)
-    per_group = [T] + counts.tolist()
+    tile = gemm_tile(rows if ep else T)
+    per_group = ([] if ep else [T]) + counts.tolist()
     gateup_units = sum((2 * F // 128) * ((c + tile - 1) // tile) for c in per_group)
     traffic = GATEUP_DRAM_BYTES_PER_UNIT * gateup_units if dominant == "gate_up" else None
     roofline = {"kernel": f"grouped_gemm_kernel ({dominant})",
@@ -328,12 +372,16 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) FP8 block-quantised experts)",
-            "config": {"workload": f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, "
-                                   f"{cfg.n_routed_experts}+1 experts resident (config 2)"
-                                   + ("; replicas per rank" if world > 1 else ""),
+            "config": {"workload": (f"1 DeepSeek-R1 MoE layer, expert-parallel over {world} GPUs "
+                                    f"({cfg.n_routed_experts // world} experts per GPU, gate and shared expert "
+                                    f"replicated), T={T} tokens per GPU, NCCL all-to-all dispatch/combine (config 3)")
+                                   if ep else
+                                   (f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, "
+                                    f"{cfg.n_routed_experts}+1 experts resident (config 2)"
+                                    + ("; independent replica per GPU" if world > 1 else "")),
                        "tokens_per_gpu": T, "hidden": H, "moe_intermediate": F, "experts": cfg.n_routed_experts, "top_k": TOPK,
                        "router": "ref", "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
-                       "parallelism": f"replica x{world}" if world > 1 else "single GPU"},
+                       "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},
             "roofline": roofline,

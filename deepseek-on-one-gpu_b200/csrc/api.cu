@@ -331,7 +331,7 @@ int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, con
 
   DSMOE_CUDA(launch_count(idx, T * K, counts, NG, s));
   DSMOE_CUDA(launch_plan(counts, NG, T, L.tile, 2 * F / 128, H / 128, row_start, cursor, us_up, us_dn, s));
-  DSMOE_CUDA(launch_quant_scatter(hidden, T, H, idx, K, 1, row_start, cursor, L.P, at<uint8_t>(ws, L.xq),
+  DSMOE_CUDA(launch_quant_scatter(hidden, T, H, idx, K, NG, 1, row_start, cursor, L.P, at<uint8_t>(ws, L.xq),
                                   at<float>(ws, L.sx), pos, s));
   prof(2, s);
 
@@ -341,7 +341,7 @@ int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, con
     return r;
 
   const float scale = c->router_mode == DSMOE_ROUTER_V3 ? 1.0f : c->routed_scaling_factor;
-  DSMOE_CUDA(launch_combine(y, T, H, pos, at<float>(ws, L.w), K, row_start, scale,
+  DSMOE_CUDA(launch_combine(y, T, H, pos, at<float>(ws, L.w), K, row_start, scale, 1,
                             static_cast<__nv_bfloat16*>(out), s));
   prof(6, s);
   return DSMOE_OK;
@@ -436,7 +436,7 @@ static int single_prologue(const void* x, int T, int K_in, int mt_up, int mt_dn,
   DSMOE_CUDA(cudaMemsetAsync(at<int32_t>(ws, L.slot0), 0, 4, s));
   DSMOE_CUDA(launch_plan(at<int32_t>(ws, L.counts), 1, T, L.tile, mt_up, mt_dn, at<int32_t>(ws, L.row_start),
                          at<int32_t>(ws, L.cursor), at<int32_t>(ws, L.us_up), at<int32_t>(ws, L.us_dn), s));
-  DSMOE_CUDA(launch_quant_scatter(x, T, K_in, nullptr, 0, 1, at<int32_t>(ws, L.row_start),
+  DSMOE_CUDA(launch_quant_scatter(x, T, K_in, nullptr, 0, 1, 1, at<int32_t>(ws, L.row_start),
                                   at<int32_t>(ws, L.cursor), L.P, at<uint8_t>(ws, L.xq), at<float>(ws, L.sx), nullptr,
                                   s));
   return DSMOE_OK;
@@ -501,6 +501,82 @@ int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_features, int32_t
   j.y = static_cast<__nv_bfloat16*>(out);
   j.status = at<int>(workspace, L.status);
   return run_gemm(j, s);
+}
+
+// ----------------------------------------------------------- expert parallel
+int dsmoe_ep_dispatch(const int64_t* topk_idx, const float* topk_w, const void* hidden, int32_t tokens,
+                      int32_t top_k, int32_t hidden_size, int32_t world, int32_t experts_per_rank,
+                      int32_t* send_counts, int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx, float* send_w,
+                      void* send_hidden, dsmoe_stream_t stream) {
+  if (tokens < 0 || top_k < 1 || top_k > 8 || world < 1 || world > 64 || experts_per_rank < 1 || hidden_size <= 0 ||
+      hidden_size % 8)
+    return fail(DSMOE_ERR_INVALID, "ep_dispatch: bad sizes (tokens %d, top_k %d, world %d, experts/rank %d)", tokens,
+                top_k, world, experts_per_rank);
+  if (tokens == 0) {
+    DSMOE_CUDA(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world, reinterpret_cast<cudaStream_t>(stream)));
+    return DSMOE_OK;
+  }
+  const void* ps[9] = {topk_idx, topk_w, hidden, send_counts, tok_rows, send_tok, send_idx, send_w, send_hidden};
+  for (const void* p : ps)
+    if (!p) return fail(DSMOE_ERR_INVALID, "ep_dispatch: NULL pointer");
+  if (!aligned16(hidden) || !aligned16(send_hidden)) return fail(DSMOE_ERR_INVALID, "ep_dispatch: unaligned rows");
+  DSMOE_CUDA(launch_ep_dispatch(topk_idx, topk_w, hidden, tokens, top_k, hidden_size, world, experts_per_rank,
+                                send_counts, tok_rows, send_tok, send_idx, send_w, send_hidden,
+                                reinterpret_cast<cudaStream_t>(stream)));
+  return DSMOE_OK;
+}
+
+size_t dsmoe_moe_local_workspace_size(const dsmoe_moe_config_t* cfg, int32_t rows) {
+  if (check_cfg(cfg) != DSMOE_OK || rows < 0) return 0;
+  return plan_moe(rows, cfg->hidden, cfg->inter, cfg->n_routed, cfg->top_k).total;
+}
+
+int dsmoe_moe_local(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden, int32_t rows,
+                    const int32_t* local_idx, const float* local_w, void* partial_out, void* workspace,
+                    size_t workspace_bytes, dsmoe_stream_t stream) {
+  int r = check_cfg(cfg);
+  if (r) return r;
+  if ((r = check_weights(cfg, w))) return r;
+  if (rows < 0) return fail(DSMOE_ERR_INVALID, "rows < 0");
+  if (rows == 0) return DSMOE_OK;
+  if (!hidden || !partial_out || !local_idx || !local_w || !aligned16(hidden) || !aligned16(partial_out))
+    return fail(DSMOE_ERR_INVALID, "moe_local: NULL or unaligned pointer");
+  const Ws L = plan_moe(rows, cfg->hidden, cfg->inter, cfg->n_routed, cfg->top_k);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(DSMOE_ERR_WORKSPACE, "workspace %zu bytes, need %zu", workspace_bytes, L.total);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int H = cfg->hidden, F = cfg->inter, K = cfg->top_k, NG = L.NG;
+  void* ws = workspace;
+  int32_t* counts = at<int32_t>(ws, L.counts);
+  int32_t* row_start = at<int32_t>(ws, L.row_start);
+  int32_t* pos = at<int32_t>(ws, L.pos);
+  DSMOE_CUDA(launch_count(local_idx, rows * K, counts, NG, s));
+  DSMOE_CUDA(launch_plan(counts, NG, 0, L.tile, 2 * F / 128, H / 128, row_start, at<int32_t>(ws, L.cursor),
+                         at<int32_t>(ws, L.us_up), at<int32_t>(ws, L.us_dn), s));
+  DSMOE_CUDA(launch_quant_scatter(hidden, rows, H, local_idx, K, NG, 0, row_start, at<int32_t>(ws, L.cursor), L.P,
+                                  at<uint8_t>(ws, L.xq), at<float>(ws, L.sx), pos, s));
+  prof(2, s);
+  __nv_bfloat16* y = at<__nv_bfloat16>(ws, L.y);
+  if ((r = run_ffn(w->w_gate, w->s_gate, w->w_up, w->s_up, w->w_down, w->s_down, w->n_slots, H, F, L, ws,
+                   w->slot_of_expert, NG, y, s)))
+    return r;
+  DSMOE_CUDA(launch_combine(y, rows, H, pos, local_w, K, row_start, 1.0f, 0,
+                            static_cast<__nv_bfloat16*>(partial_out), s));
+  prof(6, s);
+  return DSMOE_OK;
+}
+
+int dsmoe_ep_combine(const void* partials, const int32_t* tok_rows, int32_t tokens, int32_t world,
+                     int32_t hidden_size, const void* shared_out, float scale, void* out, dsmoe_stream_t stream) {
+  if (tokens < 0 || world < 1 || world > 64 || hidden_size <= 0 || hidden_size % 8)
+    return fail(DSMOE_ERR_INVALID, "ep_combine: bad sizes");
+  if (tokens == 0) return DSMOE_OK;
+  if (!tok_rows || !shared_out || !out || !aligned16(shared_out) || !aligned16(out) ||
+      (partials && !aligned16(partials)))
+    return fail(DSMOE_ERR_INVALID, "ep_combine: NULL or unaligned pointer");
+  DSMOE_CUDA(launch_ep_combine(partials, tok_rows, tokens, world, hidden_size, shared_out, scale, out,
+                               reinterpret_cast<cudaStream_t>(stream)));
+  return DSMOE_OK;
 }
 
 int dsmoe_read_status(void* workspace, int32_t* device_status, dsmoe_stream_t stream) {

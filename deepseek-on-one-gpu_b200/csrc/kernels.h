@@ -55,12 +55,20 @@ cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n
 cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int tile, int mt_up, int mt_dn,
                         int32_t* row_start, int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn,
                         cudaStream_t stream);
-cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int has_shared,
-                                 const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq, float* sx,
-                                 int32_t* pos, cudaStream_t stream);
+cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int n_groups,
+                                 int has_shared, const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq,
+                                 float* sx, int32_t* pos, cudaStream_t stream);
 
 // Combine (combine.cu)
 cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
-                           const int32_t* row_start, float scale, __nv_bfloat16* out, cudaStream_t stream);
+                           const int32_t* row_start, float scale, int has_shared, __nv_bfloat16* out,
+                           cudaStream_t stream);
+
+// Expert parallelism (ep.cu)
+cudaError_t launch_ep_dispatch(const int64_t* idx, const float* w, const void* x, int T, int K, int H, int W, int El,
+                               int32_t* counts, int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx,
+                               float* send_w, void* send_x, cudaStream_t stream);
+cudaError_t launch_ep_combine(const void* part, const int32_t* tok_rows, int T, int W, int H, const void* shared,
+                              float scale, void* out, cudaStream_t stream);
 
 }  // namespace dsmoe

@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(MAX_GROUPS) plan_kernel(int32_t* __restrict__ 
 }
 
 __global__ void __launch_bounds__(256) quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
-                                                            const int32_t* __restrict__ idx, int top_k,
+                                                            const int32_t* __restrict__ idx, int top_k, int n_groups,
                                                             int has_shared, const int32_t* __restrict__ row_start,
                                                             int32_t* __restrict__ cursor, int P,
                                                             uint8_t* __restrict__ xq, float* __restrict__ sx,
@@ -90,8 +90,8 @@ __global__ void __launch_bounds__(256) quant_scatter_kernel(const __nv_bfloat16*
   if (t >= T) return;
   int myrow = -1;
   if (lane < top_k) {
-    const int g = idx[static_cast<size_t>(t) * top_k + lane] + 1;
-    myrow = row_start[g] + atomicAdd(&cursor[g], 1);
+    const int g = idx[static_cast<size_t>(t) * top_k + lane] + 1;  // entries < 0 (no expert) are skipped
+    if (g >= 1 && g < n_groups) myrow = row_start[g] + atomicAdd(&cursor[g], 1);
     pos[static_cast<size_t>(t) * top_k + lane] = myrow;
   }
   int rows[9];
@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(256) quant_scatter_kernel(const __nv_bfloat16*
 #pragma unroll
     for (int r = 1; r < 9; ++r)
       if (r == lane) rr = rows[r];
-    sx[rr] = amax / 448.f;
+    if (rr >= 0) sx[rr] = amax / 448.f;
   }
   // pass 2: split and write every copy of the row
   for (int col = lane * 8; col < H; col += 256) {
@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(256) quant_scatter_kernel(const __nv_bfloat16*
     const uint2 lv = make_uint2(lw[0], lw[1]);
 #pragma unroll
     for (int r = 0; r < 9; ++r) {
-      if (r < n) {
+      if (r < n && rows[r] >= 0) {
         const size_t off = static_cast<size_t>(rows[r]) * H + col;
         *reinterpret_cast<uint2*>(xq + off) = hv;
         *reinterpret_cast<uint2*>(xq_lo + off) = lv;
@@ -176,13 +176,13 @@ cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int ti
   return cudaGetLastError();
 }
 
-cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int has_shared,
-                                 const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq, float* sx,
-                                 int32_t* pos, cudaStream_t stream) {
+cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int n_groups,
+                                 int has_shared, const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq,
+                                 float* sx, int32_t* pos, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   const int blocks = (T * 32 + 255) / 256;
   pm::quant_scatter_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, idx, top_k,
-                                                       has_shared, row_start, cursor, P, xq, sx, pos);
+                                                       n_groups, has_shared, row_start, cursor, P, xq, sx, pos);
   return cudaGetLastError();
 }
 

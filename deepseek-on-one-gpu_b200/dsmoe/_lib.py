@@ -22,7 +22,8 @@ EXPORTED = (
     "dsmoe_last_error", "dsmoe_version", "dsmoe_workspace_size", "dsmoe_route", "dsmoe_moe_forward",
     "dsmoe_moe_experts", "dsmoe_expert_ffn_workspace_size", "dsmoe_fp8_linear_workspace_size",
     "dsmoe_expert_ffn", "dsmoe_fp8_linear", "dsmoe_read_status", "dsmoe_set_profile_events",
-    "dsmoe_expert_ffn_noalloc",
+    "dsmoe_expert_ffn_noalloc", "dsmoe_ep_dispatch", "dsmoe_moe_local_workspace_size", "dsmoe_moe_local",
+    "dsmoe_ep_combine",
 )
 
 
@@ -76,6 +77,11 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_read_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
                 L.dsmoe_set_profile_events.argtypes = [ctypes.POINTER(vp), i32]
                 L.dsmoe_expert_ffn_noalloc.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]
+                L.dsmoe_ep_dispatch.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]
+                L.dsmoe_moe_local_workspace_size.argtypes = [cfgp, i32]
+                L.dsmoe_moe_local_workspace_size.restype = sz
+                L.dsmoe_moe_local.argtypes = [cfgp, wp, vp, i32, vp, vp, vp, vp, sz, vp]
+                L.dsmoe_ep_combine.argtypes = [vp, vp, i32, i32, i32, vp, ctypes.c_float, vp, vp]
                 for name in EXPORTED:
                     getattr(L, name).restype = getattr(L, name).restype or ctypes.c_int
                 _lib = L

@@ -1,0 +1,185 @@
+"""Expert parallelism for the MoE block (no counterpart in the single-GPU
+reference; the same arithmetic as ``inference/forward.py:112-153``).
+
+W ranks, rank r owns routed experts ``[r*El, (r+1)*El)`` (``El = E / W``); the
+gate and the shared expert are replicated, tokens stay on their rank. One
+layer step (``EPLayer.forward``):
+
+  1. route the rank's tokens (``dsmoe_route``);
+  2. ``dsmoe_ep_dispatch``: one send row per (token, owning rank), grouped by
+     destination, with the token's local expert ids and weights;
+  3. exchange counts, then rows and routing lists (all-to-all);
+  4. ``dsmoe_moe_local``: grouped FP8 GEMMs over the rank's experts for the
+     received rows, one pre-reduced bf16 row per received row;
+  5. exchange the partial rows back (all-to-all, reversed splits);
+  6. shared expert on the rank's own tokens (``dsmoe_expert_ffn``) and
+     ``dsmoe_ep_combine``: ``out = bf16(shared + bf16(scale * sum_ranks))``.
+
+The exchange is a small interface so the same step runs over
+``torch.distributed`` (NCCL between GPUs, Gloo on CPU for the bookkeeping
+tests) or over an in-process emulation of W ranks on one GPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr, stream_handle
+from .gpu_transfer import LayerBank
+from .ops import expert_ffn, route
+from .synthetic import PROJS
+
+
+class DistExchange:
+    """All-to-all over a torch.distributed process group. The per-peer row
+    counts cross the device->host boundary once per exchange (NCCL needs the
+    split sizes on the host)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+
+    def counts(self, send_counts: torch.Tensor) -> tuple[list[int], list[int]]:
+        recv = torch.empty_like(send_counts)
+        self.dist.all_to_all_single(recv, send_counts, group=self.group)
+        both = torch.cat([send_counts, recv]).tolist()
+        return both[: self.world], both[self.world:]
+
+    def rows(self, send: torch.Tensor, send_splits: list[int], recv_splits: list[int]) -> torch.Tensor:
+        out = send.new_empty((sum(recv_splits),) + tuple(send.shape[1:]))
+        self.dist.all_to_all_single(out, send[: sum(send_splits)].contiguous(), output_split_sizes=recv_splits,
+                                    input_split_sizes=send_splits, group=self.group)
+        return out
+
+
+def local_config(config, world: int):
+    """Config of one rank's share: El = E / world routed experts."""
+    E = config.n_routed_experts
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    El = E // world
+    ng = max(1, El // 32)
+    if El % 32:
+        raise ValueError("experts per rank must be a multiple of 32")
+    return config.with_(n_routed_experts=El, n_group=ng, topk_group=ng)
+
+
+class EPLayer:
+    """One MoE layer, expert-parallel. ``expert_source(layer, e)`` returns expert
+    ``e``'s ``{proj: (weight, scale)}`` (any device); by default the weight
+    store's ``get_expert``."""
+
+    def __init__(self, config, weight_store, device, layer: int, world: int, rank: int, exchange=None,
+                 expert_source=None):
+        self.config = config
+        self.store = weight_store
+        self.device = torch.device(device)
+        self.layer = layer
+        self.world, self.rank = world, rank
+        self.exchange = exchange
+        self.lcfg = local_config(config, world)
+        self.El = self.lcfg.n_routed_experts
+        src = expert_source or weight_store.get_expert
+        self.bank = LayerBank(self.lcfg, self.El + 1, self.device)
+        self.bank.write_slot(self.bank.assign(0), weight_store.get_shared_expert_weights(layer))
+        for el in range(self.El):
+            self.bank.write_slot(self.bank.assign(el + 1), src(layer, rank * self.El + el))
+        self.bank.sync_table(non_blocking=False)
+        self.shared = {p: (self.bank.w[p][0], self.bank.s[p][0]) for p in PROJS}
+        self._ws = torch.zeros(0, dtype=torch.uint8, device=self.device)
+
+    # -------------------------------------------------------------- phases
+    def dispatch(self, x: torch.Tensor):
+        """Route and pack. Returns (counts[W] int32 device, tok_rows, send_x, send_meta)."""
+        cfg = self.config
+        T, H = x.shape
+        K = cfg.num_experts_per_tok
+        bias = self.store.get_gate_bias(self.layer) if getattr(cfg, "router_mode", "ref") == "v3" else None
+        idx, w = route(x, self.store.get_gate_weight(self.layer), cfg, score_bias=bias)
+        cap = max(1, T * min(K, self.world))
+        dev = x.device
+        counts = torch.empty(self.world, dtype=torch.int32, device=dev)
+        tok_rows = torch.empty(T, self.world, dtype=torch.int32, device=dev)
+        send_tok = torch.empty(cap, dtype=torch.int32, device=dev)
+        meta = torch.empty(cap, 2 * K, dtype=torch.int32, device=dev)  # [local idx x K | weights (fp32 bits) x K]
+        send_idx = torch.empty(cap, K, dtype=torch.int32, device=dev)
+        send_w = torch.empty(cap, K, dtype=torch.float32, device=dev)
+        send_x = torch.empty(cap, H, dtype=torch.bfloat16, device=dev)
+        check(lib().dsmoe_ep_dispatch(ptr(idx), ptr(w), ptr(x), T, K, H, self.world, self.El, ptr(counts),
+                                      ptr(tok_rows), ptr(send_tok), ptr(send_idx), ptr(send_w), ptr(send_x),
+                                      stream_handle(dev)), "dsmoe_ep_dispatch")
+        meta[:, :K] = send_idx
+        meta[:, K:] = send_w.view(torch.int32)
+        return counts, tok_rows, send_x, meta
+
+    def compute(self, recv_x: torch.Tensor, recv_meta: torch.Tensor) -> torch.Tensor:
+        """The rank's experts on the received rows -> one partial row each."""
+        R, H = recv_x.shape
+        K = self.config.num_experts_per_tok
+        out = torch.empty(R, H, dtype=torch.bfloat16, device=recv_x.device)
+        if R == 0:
+            return out
+        lidx = recv_meta[:, :K].contiguous()
+        lw = recv_meta[:, K:].contiguous().view(torch.float32)
+        cfg = _lib.moe_config(self.lcfg)
+        need = lib().dsmoe_moe_local_workspace_size(cfg, R)
+        if self._ws.numel() < need:
+            self._ws = torch.zeros(int(need * 1.25) + 4096, dtype=torch.uint8, device=recv_x.device)
+        b = self.bank
+        lw_struct = _lib.LayerWeights(
+            gate_weight=None, score_bias=None, n_slots=b.n_slots,
+            w_gate=ptr(b.w["gate_proj"]), s_gate=ptr(b.s["gate_proj"]), w_up=ptr(b.w["up_proj"]),
+            s_up=ptr(b.s["up_proj"]), w_down=ptr(b.w["down_proj"]), s_down=ptr(b.s["down_proj"]),
+            slot_of_expert=ptr(b.slot_of))
+        check(lib().dsmoe_moe_local(cfg, lw_struct, ptr(recv_x), R, ptr(lidx), ptr(lw), ptr(out), ptr(self._ws),
+                                    self._ws.numel(), stream_handle(recv_x.device)), "dsmoe_moe_local")
+        return out
+
+    def finish(self, x: torch.Tensor, back: torch.Tensor, tok_rows: torch.Tensor) -> torch.Tensor:
+        """Shared expert on the rank's tokens + sum of the returned partials."""
+        T, H = x.shape
+        shared = expert_ffn(x, self.shared)
+        out = torch.empty_like(x)
+        scale = 1.0 if getattr(self.config, "router_mode", "ref") == "v3" else float(self.config.routed_scaling_factor)
+        check(lib().dsmoe_ep_combine(ptr(back) if back.numel() else None, ptr(tok_rows), T, self.world, H,
+                                     ptr(shared), scale, ptr(out), stream_handle(x.device)), "dsmoe_ep_combine")
+        return out
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """One expert-parallel MoE step for this rank's tokens ``x`` [T, H] bf16."""
+        shape = x.shape
+        x = x.reshape(-1, shape[-1]).contiguous()
+        counts, tok_rows, send_x, meta = self.dispatch(x)
+        send_splits, recv_splits = self.exchange.counts(counts)
+        recv_x = self.exchange.rows(send_x, send_splits, recv_splits)
+        recv_meta = self.exchange.rows(meta, send_splits, recv_splits)
+        part = self.compute(recv_x, recv_meta)
+        back = self.exchange.rows(part, recv_splits, send_splits)
+        return self.finish(x, back, tok_rows).view(shape)
+
+
+def emulate_step(layers: list[EPLayer], xs: list[torch.Tensor]) -> list[torch.Tensor]:
+    """Run one expert-parallel step of W ranks in one process (one device):
+    the all-to-alls become slicing and concatenation. For tests and
+    single-GPU measurements of the per-rank kernels."""
+    W = len(layers)
+    plans = [layers[r].dispatch(xs[r]) for r in range(W)]
+    counts = [p[0].tolist() for p in plans]  # counts[src][dst]
+    # rows src -> dst, in the order an all-to-all delivers them (by source rank)
+    starts = [[sum(counts[s][:d]) for d in range(W)] for s in range(W)]
+    recv_x, recv_m = [], []
+    for d in range(W):
+        recv_x.append(torch.cat([plans[s][2][starts[s][d]: starts[s][d] + counts[s][d]] for s in range(W)]))
+        recv_m.append(torch.cat([plans[s][3][starts[s][d]: starts[s][d] + counts[s][d]] for s in range(W)]))
+    parts = [layers[d].compute(recv_x[d], recv_m[d]) for d in range(W)]
+    outs = []
+    for s in range(W):
+        back = []
+        for d in range(W):
+            off = sum(counts[q][d] for q in range(s))
+            back.append(parts[d][off: off + counts[s][d]])
+        outs.append(layers[s].finish(xs[s], torch.cat(back), plans[s][1]))
+    return outs

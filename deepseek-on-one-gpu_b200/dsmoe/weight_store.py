@@ -95,23 +95,37 @@ class SyntheticWeightStore:
             self._bias[layer] = self.layer(layer).bias.to(self.device)
         return self._bias[layer]
 
+    def _generate(self, layer: int, e: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+        """Expert ``e`` (``SHARED`` for the shared expert) from the generator
+        ``gen_device`` names; every accessor below returns these same bytes."""
+        c = self.config
+        if self.gen_device == "cpu":
+            return self.layer(layer).expert(e)
+        return expert_weights(self._seed(layer), layer, e, c.hidden_size, c.moe_intermediate_size,
+                              device=self.device)
+
     def get_shared_expert_weights(self, layer: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
         if layer not in self._shared:
-            ew = self.layer(layer).shared()
+            ew = self._generate(layer, SHARED)
             self._shared[layer] = {p: (w.to(self.device), s.to(self.device)) for p, (w, s) in ew.items()}
         return self._shared[layer]
 
     def get_expert(self, layer: int, expert_idx: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
         cached = self.expert_cache.get(layer, expert_idx)
         if cached is None:
-            ew = self.layer(layer).expert(expert_idx)
+            ew = self._generate(layer, expert_idx)
             cached = {}
             for p, (w, s) in ew.items():
+                w, s = w.cpu(), s.cpu()
                 if self.pin_memory:
                     w, s = w.pin_memory(), s.pin_memory()
                 cached[p] = {"weight": w, "weight_scale_inv": s}
             self.expert_cache.put(layer, expert_idx, cached)
         return {p: (cached[p]["weight"], cached[p]["weight_scale_inv"]) for p in PROJS}
+
+    def device_expert(self, layer: int, e: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+        """Expert ``e`` on the store's device (same bytes as ``get_expert``)."""
+        return {p: (w.to(self.device), s.to(self.device)) for p, (w, s) in self._generate(layer, e).items()}
 
     def fill_bank(self, layer: int, bank, experts=None) -> None:
         """Write the shared expert and `experts` (default: all) into a device
@@ -119,12 +133,6 @@ class SyntheticWeightStore:
         by the CUDA generator (fast, but different values from the CPU
         generator that the oracle uses); with ``"cpu"`` they are the same bytes
         ``layer(l).expert(e)`` returns."""
-        c = self.config
-        experts = range(c.n_routed_experts) if experts is None else experts
+        experts = range(self.config.n_routed_experts) if experts is None else experts
         for e in [SHARED, *experts]:
-            if self.gen_device == "cpu":
-                ew = self.layer(layer).expert(e)
-            else:
-                ew = expert_weights(self._seed(layer), layer, e, c.hidden_size, c.moe_intermediate_size,
-                                    device=bank.device)
-            bank.write_slot(bank.assign(0 if e == SHARED else e + 1), ew)
+            bank.write_slot(bank.assign(0 if e == SHARED else e + 1), self.device_expert(layer, e))

@@ -151,6 +151,41 @@ DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_feature
 DSMOE_API int dsmoe_set_profile_events(void* const* events, int32_t n);
 
 /*
+ * Expert parallelism over W ranks (no counterpart in the reference, which is
+ * single-GPU; SURVEY's EP row). Rank d owns routed experts
+ * [d * experts_per_rank, (d+1) * experts_per_rank); gate and shared expert are
+ * replicated. One layer step on every rank:
+ *   1. dsmoe_route on the rank's tokens.
+ *   2. dsmoe_ep_dispatch: one send row per (token, owning rank) - a token goes
+ *      once to each rank that owns any of its experts - grouped by destination
+ *      rank, inside a rank by token id. Writes send_counts[world] (device),
+ *      tok_rows[tokens][world] (send row of each token's copy for each rank,
+ *      -1 if none), send_tok[rows], send_idx[rows][top_k] (the token's experts
+ *      on that rank as local ids in top-k order, -1 elsewhere), send_w (their
+ *      routing weights) and send_hidden[rows][hidden] (bf16 copies).
+ *      Capacity: tokens * min(top_k, world) rows.
+ *   3. The caller exchanges counts and rows (all-to-all).
+ *   4. dsmoe_moe_local on the received rows with the rank's experts (slot
+ *      table over 1 + experts_per_rank groups; group 0 unused): one bf16
+ *      partial row per received row, sum over its experts in top-k order.
+ *   5. The caller returns the partial rows (all-to-all back, same splits).
+ *   6. dsmoe_ep_combine: out[t] = bf16(shared[t] + bf16(scale * sum)), the sum
+ *      over the returned rows of token t in rank order (bf16), shared[t] the
+ *      shared expert on the rank's own tokens (dsmoe_expert_ffn).
+ */
+DSMOE_API int dsmoe_ep_dispatch(const int64_t* topk_idx, const float* topk_w, const void* hidden, int32_t tokens,
+                                int32_t top_k, int32_t hidden_size, int32_t world, int32_t experts_per_rank,
+                                int32_t* send_counts, int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx,
+                                float* send_w, void* send_hidden, dsmoe_stream_t stream);
+DSMOE_API size_t dsmoe_moe_local_workspace_size(const dsmoe_moe_config_t* cfg_local, int32_t rows);
+DSMOE_API int dsmoe_moe_local(const dsmoe_moe_config_t* cfg_local, const dsmoe_layer_weights_t* w, const void* hidden,
+                              int32_t rows, const int32_t* local_idx, const float* local_w, void* partial_out,
+                              void* workspace, size_t workspace_bytes, dsmoe_stream_t stream);
+DSMOE_API int dsmoe_ep_combine(const void* partials, const int32_t* tok_rows, int32_t tokens, int32_t world,
+                               int32_t hidden_size, const void* shared_out, float scale, void* out,
+                               dsmoe_stream_t stream);
+
+/*
  * Allocation-free variant of dsmoe_expert_ffn (no counterpart in the
  * reference; an addition of this library).
  *

@@ -1,0 +1,64 @@
+"""The expert-parallel exchange (dsmoe.ep.DistExchange) on CPU with two Gloo
+ranks: count exchange, variable-split all-to-all there and back."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "deepseek-on-one-gpu_b200"))
+    from dsmoe.ep import DistExchange
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        ex = DistExchange()
+        # rank r sends (r + d + 1) rows to rank d, each row = [src, dst, i] * 4
+        send_counts = torch.tensor([rank + d + 1 for d in range(world)], dtype=torch.int32)
+        rows = [torch.tensor([rank, d, i, 7] * 4, dtype=torch.int32) for d in range(world)
+                for i in range(rank + d + 1)]
+        send = torch.stack(rows + [torch.full((16,), -9, dtype=torch.int32)])  # one unused capacity row
+        sc, rc = ex.counts(send_counts)
+        assert sc == [rank + d + 1 for d in range(world)]
+        assert rc == [s + rank + 1 for s in range(world)]
+        recv = ex.rows(send, sc, rc)
+        off = 0
+        for s in range(world):
+            for i in range(rc[s]):
+                assert recv[off].tolist()[:3] == [s, rank, i]
+                off += 1
+        back = ex.rows(recv * 2, rc, sc)  # the partial rows go back in the senders' order
+        assert torch.equal(back, send[: sum(sc)] * 2)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+def test_dist_exchange_two_gloo_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: "ok", 1: "ok"}

@@ -1,0 +1,70 @@
+"""Expert-parallel step (dsmoe.ep) on one GPU: W ranks emulated in one process
+(the all-to-alls become slicing), each rank's output compared with the
+single-GPU moe_block on the same tokens and with the CPU oracle."""
+import pytest
+import torch
+
+from dsmoe import DeepSeekConfig, GPUTransfer, SyntheticWeightStore, moe_block
+from dsmoe.ep import EPLayer, emulate_step
+from dsmoe.synthetic import activations
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+REL_RMS_TOL = 1e-2
+
+
+@pytest.mark.parametrize("W,T,mode", [(2, 64, "ref"), (4, 96, "ref"), (8, 40, "ref"), (8, 300, "v3"), (1, 33, "ref")])
+def test_ep_emulated_matches_single_gpu(W, T, mode):
+    H, F = 512, 256
+    cfg = DeepSeekConfig(hidden_size=H, moe_intermediate_size=F, router_mode=mode)
+    store = SyntheticWeightStore(cfg, seed=31, device=DEV, pin_memory=False, gen_device="cpu",
+                                 bias_zipf=1.1 if mode == "v3" else None)
+    layers = [EPLayer(cfg, store, DEV, 3, W, r, expert_source=store.device_expert) for r in range(W)]
+    xs = [activations(40 + r, T, H).to(DEV) for r in range(W)]
+    outs = emulate_step(layers, xs)
+    gt = GPUTransfer(cfg, store, DEV)
+    L = store.layer(3)
+    for r in range(W):
+        single = moe_block(xs[r], 3, store, gt, cfg)
+        assert O.rel_rms(outs[r].float().cpu(), single.float().cpu()) < 5e-3
+        x = xs[r].cpu()
+        if mode == "v3":
+            idx, w = O.route_v3(x, L.gate, L.bias)
+            ref = O.moe_block_grouped(x, idx, w, L.expert, L.shared(), final_scale=1.0)
+        else:
+            idx, w = O.route_ref(x, L.gate)
+            ref = O.moe_block_grouped(x, idx, w, L.expert, L.shared())
+        assert O.rel_rms(outs[r].float().cpu(), ref.float()) < REL_RMS_TOL
+
+
+def test_ep_full_dims_w8():
+    cfg = DeepSeekConfig()
+    store = SyntheticWeightStore(cfg, seed=41, device=DEV, pin_memory=False, gen_device="cuda")
+    W, T = 8, 128
+    layers = [EPLayer(cfg, store, DEV, 3, W, r, expert_source=store.device_expert) for r in range(W)]
+    xs = [activations(50 + r, T, 7168).to(DEV) for r in range(W)]
+    outs = emulate_step(layers, xs)
+    gt = GPUTransfer(cfg, store, DEV)
+    for r in (0, 5):
+        single = moe_block(xs[r], 3, store, gt, cfg)
+        assert O.rel_rms(outs[r].float().cpu(), single.float().cpu()) < 5e-3
+    assert all(torch.isfinite(o.float()).all() for o in outs)
+
+
+def test_ep_rank_with_no_tokens_for_it():
+    """A rank that receives nothing (all tokens routed elsewhere) still returns."""
+    H, F = 256, 128
+    cfg = DeepSeekConfig(hidden_size=H, moe_intermediate_size=F)
+    store = SyntheticWeightStore(cfg, seed=5, device=DEV, pin_memory=False, gen_device="cpu")
+    gate = torch.zeros(256, H)
+    gate[[0, 1, 2, 3, 4, 5, 6, 7]] = 0.05  # experts 0-7 live on rank 0 of 8
+    store._gate[3] = gate.to(torch.bfloat16).to(DEV)
+    W = 8
+    layers = [EPLayer(cfg, store, DEV, 3, W, r, expert_source=store.device_expert) for r in range(W)]
+    xs = [activations(60 + r, 16, H).abs().to(DEV) for r in range(W)]
+    outs = emulate_step(layers, xs)
+    gt = GPUTransfer(cfg, store, DEV)
+    for r in range(W):
+        single = moe_block(xs[r], 3, store, gt, cfg)
+        assert O.rel_rms(outs[r].float().cpu(), single.float().cpu()) < 5e-3

@@ -1,0 +1,71 @@
+"""Expert parallelism across real GPUs (NCCL all-to-all): 2 ranks as
+processes, each rank's output compared with the single-GPU moe_block on the
+same tokens. Skipped when fewer than 2 GPUs are visible."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, q):
+    import sys
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "deepseek-on-one-gpu_b200"))
+    sys.path.insert(0, root)
+    from dsmoe import DeepSeekConfig, GPUTransfer, SyntheticWeightStore, moe_block
+    from dsmoe.ep import DistExchange, EPLayer
+    from dsmoe.synthetic import activations
+    from oracle.moe_oracle import rel_rms
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        cfg = DeepSeekConfig(hidden_size=512, moe_intermediate_size=256)
+        store = SyntheticWeightStore(cfg, seed=77, device=dev, pin_memory=False, gen_device="cpu")
+        layer = EPLayer(cfg, store, dev, 3, world, rank, exchange=DistExchange(), expert_source=store.device_expert)
+        results = []
+        for step, T in enumerate((64, 200, 1)):
+            x = activations(100 * step + rank, T, 512).to(dev)
+            out = layer.forward(x)
+            single = moe_block(x, 3, store, GPUTransfer(cfg, store, dev), cfg)
+            results.append(rel_rms(out.float().cpu(), single.float().cpu()))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, results))
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_ranks_nccl():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
+        assert isinstance(res[r], list), res[r]
+        assert max(res[r]) < 5e-3, res[r]
