@@ -278,8 +278,6 @@ def main():
             ep_layer.finish(x, ep_layer.exchange.rows(part, rc, sc), tok_rows)
             torch.cuda.synchronize()
             set_profile_events(evs)
-            from dsmoe.ops import route as _route
-            idx, _w = _route(x, store.get_gate_weight(LAYER), cfg)
         else:
             out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)
         torch.cuda.synchronize()

@@ -41,11 +41,12 @@ def _rank_main(rank, world, port, q):
         cfg = DeepSeekConfig(hidden_size=512, moe_intermediate_size=256)
         store = SyntheticWeightStore(cfg, seed=77, device=dev, pin_memory=False, gen_device="cpu")
         layer = EPLayer(cfg, store, dev, 3, world, rank, exchange=DistExchange(), expert_source=store.device_expert)
+        gt = GPUTransfer(cfg, store, dev)
         results = []
         for step, T in enumerate((64, 200, 1)):
             x = activations(100 * step + rank, T, 512).to(dev)
             out = layer.forward(x)
-            single = moe_block(x, 3, store, GPUTransfer(cfg, store, dev), cfg)
+            single = moe_block(x, 3, store, gt, cfg)
             results.append(rel_rms(out.float().cpu(), single.float().cpu()))
         dist.barrier()
         dist.destroy_process_group()
