@@ -165,14 +165,103 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_streaming(args, rank, world, local):
+    """Config 5: B=1 decode steps through 8 MoE layers (seeds 10..17), all
+    routed experts in pinned host memory, a 64-expert GPU slot cache per layer
+    (+ the shared expert), next-layer prefetch on a side stream."""
+    from dsmoe import DeepSeekConfig, SyntheticWeightStore
+    from dsmoe.streaming import StreamingDecoder
+    from dsmoe.synthetic import activations
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    layers = list(range(8))
+    cfg = DeepSeekConfig()
+    store = SyntheticWeightStore(cfg, seed=10, device=dev, pin_memory=True, gen_device="cuda",
+                                 layer_seeds={l: 10 + l for l in layers}, expert_cache_bytes=1 << 40)
+    t0 = time.perf_counter()
+    pinned = store.preload_host(layers)
+    setup_s = time.perf_counter() - t0
+    # host-link reference: one pinned -> device copy of 1 GiB
+    src = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty_like(src, device=dev)
+    for _ in range(2):
+        dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(3):
+        dst.copy_(src, non_blocking=True)
+    c1.record()
+    torch.cuda.synchronize()
+    link_gbs = 3 * src.nbytes / (c0.elapsed_time(c1) / 1e3) / 1e9
+    del src, dst
+    dec = StreamingDecoder(cfg, store, dev, layers, slots_per_layer=65, prefetch=not args.no_prefetch)
+    # a new token every step (N(0,1) hidden state), carried through the 8 layers
+    h_host = activations(10, args.warmup + args.steps, H).pin_memory()
+    out_host = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
+    for i in range(args.warmup):
+        dec.step(h_host[i:i + 1].to(dev))
+    torch.cuda.synchronize()
+    b0, m0, hit0 = dec.gt.bytes_h2d, dec.gt.slot_misses, dec.gt.slot_hits
+    p0, u0 = dec.predicted, dec.predicted_used
+    steps = args.steps
+    sampler = ClockSampler({local})
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        hd = h_host[args.warmup + i: args.warmup + i + 1].to(dev, non_blocking=True)  # the token in
+        h = dec.step(hd)
+        out_host.copy_(h, non_blocking=True)  # its final hidden state out
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / steps
+    moved = dec.gt.bytes_h2d - b0
+    misses, hits = dec.gt.slot_misses - m0, dec.gt.slot_hits - hit0
+    achieved = moved / (steps * ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": 1e3 / ms, "unit": UNIT, "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
+        "data": "synthetic (seeded; per-layer seeds 10..17)",
+        "config": {"workload": "B=1 decode through 8 DeepSeek-R1 MoE layers, experts in pinned host memory "
+                               "(config 5), h <- h + moe(h) per layer",
+                   "slots_per_layer": 64, "prefetch": not args.no_prefetch, "pinned_host_gb": pinned / 1e9,
+                   "host_setup_s": setup_s, "baseline_config": 5},
+        "e2e": {"value": 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
+        "roofline": {"kernel": "expert H2D copies (host link)", "bound": "host-link", "achieved": achieved,
+                     "peak": link_gbs, "unit": "GB/s", "frac": achieved / link_gbs,
+                     "peak_source": "measured pinned->device copy of 1 GiB in this run", "traffic": None},
+        "streaming": {"h2d_gb_per_step": moved / steps / 1e9, "slot_hit_rate": hits / max(1, hits + misses),
+                      "misses_per_layer_step": misses / (steps * len(layers)),
+                      "prefetch_precision": (dec.predicted_used - u0) / max(1, dec.predicted - p0),
+                      "prefetched_experts": dec.gt.prefetched},
+        "gpu_launches": 9 * len(layers) * steps,
+        "clocks": clocks,
+        "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="dsmoe", choices=["dsmoe", "reference"])
-    ap.add_argument("--tokens", type=int, default=None,
-                    help="tokens per GPU (default 4096 on 1 GPU - config 2; 8192 per GPU expert-parallel - config 3)")
+    ap.add_argument("--config", type=int, default=None, choices=[2, 3, 4, 5],
+                    help="BASELINE config: 2 = prefill T=4096 on 1 GPU (default at N=1), 3 = expert-parallel "
+                         "T=8192 per GPU (default at N>1), 4 = load skew: bias-corrected router with Zipf(1.1) "
+                         "bias, T=16384 per GPU, 5 = streaming decode through 8 layers with experts in pinned "
+                         "host memory (1 GPU)")
+    ap.add_argument("--no-prefetch", action="store_true",
+                    help="config 5: no next-layer expert prediction (default: adaptive prefetch)")
+    ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (default: the config's)")
     ap.add_argument("--mode", default="ep", choices=["ep", "replica"],
                     help="N > 1: expert-parallel over NCCL (default) or independent replicas")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
@@ -187,10 +276,16 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.config is None:
+        args.config = 2 if world == 1 else 3
     if args.tokens is None:
-        args.tokens = 4096 if world == 1 else 8192
+        args.tokens = {2: 4096, 3: 8192, 4: 16384, 5: 1}[args.config]
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+
+    if args.config == 5:
+        run_streaming(args, rank, world, local)
         return
 
     import torch.distributed as dist
@@ -207,26 +302,31 @@ def main():
 
     T = args.tokens
     n_group = max(1, args.experts // 32)
-    cfg = DeepSeekConfig(n_routed_experts=32 * n_group, n_group=n_group, topk_group=min(4, n_group))
+    skew = args.config == 4
+    cfg = DeepSeekConfig(n_routed_experts=32 * n_group, n_group=n_group, topk_group=min(4, n_group),
+                         router_mode="v3" if skew else "ref")
+    zipf = 1.1 if skew else None
+    seed = {2: 1, 3: 2, 4: 3}[args.config]
     ep = world > 1 and args.mode == "ep"
     if ep:
-        # config 3: one set of layer weights (seed 2) sharded over the ranks,
-        # every rank with its own 8192 tokens
+        # one set of layer weights sharded over the ranks, every rank with its
+        # own tokens
         from dsmoe.ep import DistExchange, EPLayer
 
-        store = SyntheticWeightStore(cfg, seed=2, device=dev, pin_memory=False, gen_device="cuda")
+        store = SyntheticWeightStore(cfg, seed=seed, device=dev, pin_memory=False, gen_device="cuda", bias_zipf=zipf)
         ep_layer = EPLayer(cfg, store, dev, LAYER, world, rank, exchange=DistExchange(),
                            expert_source=store.device_expert)
         bank = None
-        x = activations(2000 + rank, T, H, device=dev)
+        x = activations(1000 * seed + rank, T, H, device=dev)
 
         def step(inp):
             return ep_layer.forward(inp)
     else:
-        store = SyntheticWeightStore(cfg, seed=1 + rank, device=dev, pin_memory=False, gen_device="cuda")
+        store = SyntheticWeightStore(cfg, seed=seed + rank, device=dev, pin_memory=False, gen_device="cuda",
+                                     bias_zipf=zipf)
         gt = GPUTransfer(cfg, store, dev)
         bank = gt.bank(LAYER)
-        x = activations(1 + rank, T, H, device=dev)
+        x = activations(seed + rank, T, H, device=dev)
 
         def step(inp):
             return moe_block(inp, LAYER, store, gt, cfg)
@@ -284,6 +384,11 @@ def main():
         for i in range(len(names)):
             stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
     set_profile_events(None)
+    from dsmoe.ops import route as _route
+    _gidx, _ = _route(x, store.get_gate_weight(LAYER), cfg,
+                      score_bias=store.get_gate_bias(LAYER) if skew else None)
+    gcounts = torch.bincount(_gidx.reshape(-1), minlength=cfg.n_routed_experts).float()
+    hottest_over_mean = float(gcounts.max() / gcounts.mean())
     if ep:
         # the rank's own GEMM work: its experts over the rows it received (no shared expert there)
         lidx = recv_meta[:, :TOPK].reshape(-1)
@@ -372,13 +477,16 @@ def main():
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) FP8 block-quantised experts)",
             "config": {"workload": (f"1 DeepSeek-R1 MoE layer, expert-parallel over {world} GPUs "
                                     f"({cfg.n_routed_experts // world} experts per GPU, gate and shared expert "
-                                    f"replicated), T={T} tokens per GPU, NCCL all-to-all dispatch/combine (config 3)")
+                                    f"replicated), T={T} tokens per GPU, NCCL all-to-all dispatch/combine "
+                                    f"(config {args.config})")
                                    if ep else
                                    (f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, "
-                                    f"{cfg.n_routed_experts}+1 experts resident (config 2)"
+                                    f"{cfg.n_routed_experts}+1 experts resident (config {args.config})"
                                     + ("; independent replica per GPU" if world > 1 else "")),
                        "tokens_per_gpu": T, "hidden": H, "moe_intermediate": F, "experts": cfg.n_routed_experts, "top_k": TOPK,
-                       "router": "ref", "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
+                       "router": cfg.router_mode, "baseline_config": args.config,
+                       "hottest_expert_over_mean": hottest_over_mean,
+                       "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
                        "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},

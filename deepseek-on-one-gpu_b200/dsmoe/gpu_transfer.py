@@ -47,6 +47,7 @@ class LayerBank:
         self.lru: OrderedDict[int, int] = OrderedDict()  # group -> slot, routed experts only
         self.free = list(range(n_slots))
         self.last_use: torch.cuda.Event | None = None
+        self.pending: torch.cuda.Event | None = None  # prefetch copies in flight
         self.dirty = False
 
     @property
@@ -117,6 +118,7 @@ class GPUTransfer:
         self.bytes_h2d = 0
         self.slot_hits = 0
         self.slot_misses = 0
+        self.prefetched = 0
 
     @property
     def resident(self) -> bool:
@@ -138,11 +140,37 @@ class GPUTransfer:
             torch.cuda.current_stream(self.device).synchronize()
         return b
 
+    def prefetch(self, layer: int, experts) -> int:
+        """Start bringing `experts` (routed ids) into the layer's bank on the side
+        stream without making the compute stream wait; the next
+        ``ensure_resident`` on this layer waits for them. Returns the number of
+        experts whose copy was started."""
+        b = self.bank(layer)
+        missing = [g for g in dict.fromkeys(int(e) + 1 for e in experts) if b.slot_of_host[g] < 0]
+        if not missing:
+            return 0
+        ts = self.transfer_stream
+        if b.last_use is not None:
+            ts.wait_event(b.last_use)
+        with torch.cuda.stream(ts):
+            for g in missing:
+                slot = b.assign(g, pinned=set(missing))
+                self.bytes_h2d += b.write_slot(slot, self.weight_store.get_expert(layer, g - 1), non_blocking=True)
+            b.sync_table(non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(ts)
+        b.pending = ev
+        self.prefetched += len(missing)
+        return len(missing)
+
     def ensure_resident(self, layer: int, experts) -> LayerBank:
         """Make `experts` (routed ids) resident in the layer's bank. Copies run
         on the side stream after the bank's last use; the current stream waits
-        for them with an event."""
+        for them (and for any prefetch of this layer) with an event."""
         b = self.bank(layer)
+        if b.pending is not None:
+            torch.cuda.current_stream(self.device).wait_event(b.pending)
+            b.pending = None
         need = [int(e) for e in experts]
         groups = {e + 1 for e in need}
         missing = [g for g in dict.fromkeys(e + 1 for e in need) if b.slot_of_host[g] < 0]

@@ -123,6 +123,38 @@ class SyntheticWeightStore:
             self.expert_cache.put(layer, expert_idx, cached)
         return {p: (cached[p]["weight"], cached[p]["weight_scale_inv"]) for p in PROJS}
 
+    def preload_host(self, layers) -> int:
+        """Fill the pinned host LRU with every routed expert of `layers` (the
+        host-resident expert store of the streaming configuration): one pinned
+        arena per layer, experts generated by ``gen_device`` and copied straight
+        into it. Returns the pinned bytes."""
+        c = self.config
+        E, H, F = c.n_routed_experts, c.hidden_size, c.moe_intermediate_size
+        wbytes = {"gate_proj": F * H, "up_proj": F * H, "down_proj": H * F}
+        sshape = {"gate_proj": (F // 128, H // 128), "up_proj": (F // 128, H // 128), "down_proj": (H // 128, F // 128)}
+        per_w = sum(wbytes.values())
+        per_s = sum(a * b for a, b in sshape.values())
+        total = 0
+        for layer in layers:
+            warena = torch.empty(E * per_w, dtype=torch.uint8, pin_memory=self.pin_memory)
+            sarena = torch.empty(E * per_s, dtype=torch.float32, pin_memory=self.pin_memory)
+            total += warena.nbytes + sarena.nbytes
+            for e in range(E):
+                ew = self._generate(layer, e)
+                wo, so = e * per_w, e * per_s
+                entry = {}
+                for p in PROJS:
+                    w, sc = ew[p]
+                    hw = warena[wo: wo + wbytes[p]].view(torch.float8_e4m3fn).view(w.shape)
+                    hs = sarena[so: so + sc.numel()].view(sc.shape)
+                    hw.copy_(w)
+                    hs.copy_(sc)
+                    wo += wbytes[p]
+                    so += sc.numel()
+                    entry[p] = {"weight": hw, "weight_scale_inv": hs}
+                self.expert_cache.put(layer, e, entry)
+        return total
+
     def device_expert(self, layer: int, e: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
         """Expert ``e`` on the store's device (same bytes as ``get_expert``)."""
         return {p: (w.to(self.device), s.to(self.device)) for p, (w, s) in self._generate(layer, e).items()}
