@@ -33,14 +33,23 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
   const int srow = row_start[0] + t;
   const int nchunks = H / 8;
   for (int c = threadIdx.x; c < nchunks; c += blockDim.x) {
+    // All rows of the token are loaded before the ordered bf16 sum so that
+    // the loads overlap.
+    uint4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = k < top_k ? s_row[k] : -1;
+      v[k] = r >= 0 ? __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(r) * H) + c) : make_uint4(0, 0, 0, 0);
+    }
+    const uint4 sv = has_shared ? __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(srow) * H) + c)
+                                : make_uint4(0, 0, 0, 0);
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int k = 0; k < top_k; ++k) {
-      const int r = s_row[k];
-      if (r < 0) continue;
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(r) * H) + c);
-      const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k >= top_k || s_row[k] < 0) continue;
+      const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v[k]);
       const float wk = s_w[k];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = bf16_round(acc[i] + bf16_round(wk * __bfloat162float(vb[i])));
@@ -48,7 +57,6 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
     uint4 o;
     __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
     if (has_shared) {
-      const uint4 sv = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(srow) * H) + c);
       const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(&sv);
 #pragma unroll
       for (int i = 0; i < 8; ++i)

@@ -24,13 +24,19 @@
 // tiles 0..F/128-1 read the gate bank, the rest the up bank) and the output
 // row is [g | u] (2F wide); swiglu_quant.cu forms h = silu(g) * u.
 //
-// Warp roles (576 threads, one CTA per SM, persistent over work units):
+// Warp roles (608 threads, one CTA per SM, persistent over work units):
 //   warp 0      TMA producer (one thread)
-//   warp 1      TMEM allocator + MMA issuer (one thread)
+//   warp 1      TMEM allocator + MMA issuer for even K steps (one thread)
 //   warps 2-17  epilogue: warp w reads TMEM lane quadrant (w % 4) and the
 //               column group ((w - 2) / 4) of BN / 4 accumulator columns.
+//   warp 18     MMA issuer for odd K steps (one thread)
+// Two issuers: a thread that waits on an mbarrier between its MMA batches
+// leaves the tensor pipe idle for a few hundred cycles each time; with the
+// K steps split by parity one issuer's MMAs run while the other waits. Every
+// K step writes its own TMEM buffer and smem stage, so the two streams are
+// independent; each issuer commits only its own MMAs.
 // The SM's register file is split over four 16K-register sub-partitions and
-// 18 warps put 5 warps on one of them, so the kernel is capped at 96
+// 19 warps put 5 warps on some of them, so the kernel is capped at 96
 // registers per thread.
 // Activation tiles are one TMA box of BN rows per term (hi, lo); groups of at
 // most 64 tokens use 32-row boxes instead so decode steps do not pull BN rows.
@@ -46,7 +52,9 @@ constexpr int BM = 128;   // weight rows (output features) per tile
 constexpr int BK = 128;   // K bytes per stage
 constexpr int SUB = 32;   // token rows per small activation TMA box
 constexpr int NUM_EPI_WARPS = 16;
-constexpr int NUM_THREADS = (2 + NUM_EPI_WARPS) * 32;
+constexpr int NUM_MMA_ISSUERS = 2;
+constexpr int NUM_THREADS = (2 + NUM_EPI_WARPS + 1) * 32;
+constexpr int ISSUER_B_WARP = 2 + NUM_EPI_WARPS;
 constexpr int MAX_GROUPS = 264;
 
 template <int BN_, int STAGES_, int NBUF_, bool NCAT_>
@@ -140,7 +148,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], NUM_EPI_WARPS);
     }
-    mbar_init(done_bar, 1);
+    mbar_init(done_bar, NUM_MMA_ISSUERS);
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -214,9 +222,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         mbar_wait(&full[stage], phase, p.status, kDevTimeoutProducer, s_abort);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == ISSUER_B_WARP) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
+      const int me = warp == 1 ? 0 : 1;  // issues the K steps of this parity
+      int step = 0;
       int stage = 0;
       uint32_t phase = 0;
       int tb = 0;
@@ -228,7 +238,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         const int ncols = min(BN, s_counts[g] - nt * BN);
         const int N = C::NCAT ? 2 * BN : (ncols + 15) & ~15;
         const uint32_t idesc = idesc_e4m3(BM, N);
-        for (int kb = 0; kb < n_kb; ++kb) {
+        for (int kb = 0; kb < n_kb; ++kb, ++step) {
+          if ((step & 1) != me) {  // the other issuer's step: only advance the rings
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            if (++tb == NBUF) { tb = 0; tphase ^= 1; }
+            continue;
+          }
           if (!mbar_wait(&tempty[tb], tphase ^ 1, p.status, kDevTimeoutMma, s_abort)) { ok = false; break; }
           if (!mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma, s_abort)) { ok = false; break; }
           tc_fence_after();
@@ -255,11 +270,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
           if (++tb == NBUF) { tb = 0; tphase ^= 1; }
         }
       }
-      // All MMAs issued by this thread complete before TMEM is released.
+      // All MMAs of both issuers complete before TMEM is released (the
+      // barrier's first phase needs one commit from each).
       mma_commit(done_bar);
       mbar_wait(done_bar, 0, p.status, kDevTimeoutMma, s_abort);
     }
-  } else {
+  } else if (warp >= 2 && warp < 2 + NUM_EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;
     const int cg = (warp - 2) >> 2;

@@ -6,8 +6,11 @@
 //                                             reference's F.silu on bf16 and
 //                                             the bf16 product)
 // and stores it in the down GEMM's activation format: one fp32 scale per row
-// and two e4m3 terms, h ~= (hi + lo) * scale. One warp per row, two passes
-// (row amax, then the split; the second pass re-reads g and u from L1/L2).
+// and two e4m3 terms, h ~= (hi + lo) * scale. One warp per row. Rows of up to
+// 2048 features are done in one pass: every lane loads all of its g and u
+// vectors first (16 loads in flight), and keeps its 64 values of h packed in
+// 32 registers (h is exactly representable in bf16) while the warp reduces
+// the row amax. Wider rows take two passes (the second re-reads g and u).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,6 +28,86 @@ __device__ __forceinline__ void swiglu8(const __nv_bfloat16* g, const __nv_bfloa
 #pragma unroll
   for (int i = 0; i < 8; ++i)
     h[i] = bf16_round(bf16_round(silu_f32(__bfloat162float(gb[i]))) * __bfloat162float(ub[i]));
+}
+
+// Split 8 values (already multiplied by 448 / amax) into hi and lo e4m3 terms
+// and store them at hi_dst / lo_dst.
+__device__ __forceinline__ void split_store8(const float* q, uint8_t* hi_dst, uint8_t* lo_dst) {
+  uint32_t hw[2], lw[2];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const uint16_t h2 = f32x2_to_e4m3x2(q[i], q[i + 1]);
+    const uint16_t l2 = f32x2_to_e4m3x2(q[i] - e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff)),
+                                        q[i + 1] - e4m3_to_f32(static_cast<uint8_t>(h2 >> 8)));
+    if ((i & 2) == 0) {
+      hw[i >> 2] = h2;
+      lw[i >> 2] = l2;
+    } else {
+      hw[i >> 2] |= static_cast<uint32_t>(h2) << 16;
+      lw[i >> 2] |= static_cast<uint32_t>(l2) << 16;
+    }
+  }
+  *reinterpret_cast<uint2*>(hi_dst) = make_uint2(hw[0], hw[1]);
+  *reinterpret_cast<uint2*>(lo_dst) = make_uint2(lw[0], lw[1]);
+}
+
+// One pass, F <= 256 * NIT.
+template <int NIT>
+__global__ void __launch_bounds__(256) swiglu_quant_1pass(const __nv_bfloat16* __restrict__ gu, int F,
+                                                          const int32_t* __restrict__ row_end, int P,
+                                                          uint8_t* __restrict__ hq, float* __restrict__ hs) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= *row_end) return;
+  const __nv_bfloat16* g_row = gu + static_cast<size_t>(row) * 2 * F;
+  const __nv_bfloat16* u_row = g_row + F;
+  uint4 gv[NIT], uv[NIT];
+#pragma unroll
+  for (int it = 0; it < NIT; ++it) {
+    const int col = it * 256 + lane * 8;
+    if (col < F) {
+      gv[it] = __ldg(reinterpret_cast<const uint4*>(g_row + col));
+      uv[it] = __ldg(reinterpret_cast<const uint4*>(u_row + col));
+    }
+  }
+  __nv_bfloat162 hb[NIT * 4];
+  float amax = 0.f;
+#pragma unroll
+  for (int it = 0; it < NIT; ++it) {
+    const int col = it * 256 + lane * 8;
+    if (col < F) {
+      const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv[it]);
+      const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uv[it]);
+      float h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        h[i] = bf16_round(bf16_round(silu_f32(__bfloat162float(gb[i]))) * __bfloat162float(ub[i]));
+        amax = fmaxf(amax, fabsf(h[i]));
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hb[it * 4 + i] = __floats2bfloat162_rn(h[2 * i], h[2 * i + 1]);  // exact
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float inv = amax > 0.f ? 448.f / amax : 0.f;
+  if (lane == 0) hs[row] = amax / 448.f;
+  uint8_t* hi_row = hq + static_cast<size_t>(row) * F;
+  uint8_t* lo_row = hq + (static_cast<size_t>(P) + row) * F;
+#pragma unroll
+  for (int it = 0; it < NIT; ++it) {
+    const int col = it * 256 + lane * 8;
+    if (col < F) {
+      float q[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 v = __bfloat1622float2(hb[it * 4 + i]);
+        q[2 * i] = v.x * inv;
+        q[2 * i + 1] = v.y * inv;
+      }
+      split_store8(q, hi_row + col, lo_row + col);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ gu, int F,
@@ -51,23 +134,9 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* 
   for (int col = lane * 8; col < F; col += 256) {
     float h[8];
     swiglu8(g_row + col, u_row + col, h);
-    uint32_t hw[2], lw[2];
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      const float q0 = h[i] * inv, q1 = h[i + 1] * inv;
-      const uint16_t h2 = f32x2_to_e4m3x2(q0, q1);
-      const uint16_t l2 = f32x2_to_e4m3x2(q0 - e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff)),
-                                          q1 - e4m3_to_f32(static_cast<uint8_t>(h2 >> 8)));
-      if ((i & 2) == 0) {
-        hw[i >> 2] = h2;
-        lw[i >> 2] = l2;
-      } else {
-        hw[i >> 2] |= static_cast<uint32_t>(h2) << 16;
-        lw[i >> 2] |= static_cast<uint32_t>(l2) << 16;
-      }
-    }
-    *reinterpret_cast<uint2*>(hi_row + col) = make_uint2(hw[0], hw[1]);
-    *reinterpret_cast<uint2*>(lo_row + col) = make_uint2(lw[0], lw[1]);
+    for (int i = 0; i < 8; ++i) h[i] *= inv;
+    split_store8(h, hi_row + col, lo_row + col);
   }
 }
 }  // namespace sq
@@ -76,7 +145,10 @@ cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* r
                                 float* hs, cudaStream_t stream) {
   if (P == 0) return cudaSuccess;
   const int blocks = (P * 32 + 255) / 256;
-  sq::swiglu_quant_kernel<<<blocks, 256, 0, stream>>>(gu, F, row_end, P, hq, hs);
+  if (F <= 2048)
+    sq::swiglu_quant_1pass<8><<<blocks, 256, 0, stream>>>(gu, F, row_end, P, hq, hs);
+  else
+    sq::swiglu_quant_kernel<<<blocks, 256, 0, stream>>>(gu, F, row_end, P, hq, hs);
   return cudaGetLastError();
 }
 
