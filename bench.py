@@ -264,6 +264,12 @@ def main():
     ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (default: the config's)")
     ap.add_argument("--mode", default="ep", choices=["ep", "replica"],
                     help="N > 1: expert-parallel over NCCL (default) or independent replicas")
+    ap.add_argument("--chunks", type=int, default=1,
+                    help="expert-parallel step: token chunks whose all-to-alls overlap the expert GEMMs (1 = none)")
+    ap.add_argument("--sm-reserve", type=int, default=16,
+                    help="expert-parallel step: SMs the grouped GEMMs leave to the all-to-alls while they overlap")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="expert-parallel step: exchange and GEMMs in one stream, one after the other")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--ref-tokens-per-step", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -316,11 +322,13 @@ def main():
         store = SyntheticWeightStore(cfg, seed=seed, device=dev, pin_memory=False, gen_device="cuda", bias_zipf=zipf)
         ep_layer = EPLayer(cfg, store, dev, LAYER, world, rank, exchange=DistExchange(),
                            expert_source=store.device_expert)
+        ep_layer.sm_reserve = args.sm_reserve
+        ep_layer.overlap = not args.no_overlap
         bank = None
         x = activations(1000 * seed + rank, T, H, device=dev)
 
         def step(inp):
-            return ep_layer.forward(inp)
+            return ep_layer.forward(inp, chunks=args.chunks)
     else:
         store = SyntheticWeightStore(cfg, seed=seed + rank, device=dev, pin_memory=False, gen_device="cuda",
                                      bias_zipf=zipf)
@@ -384,6 +392,38 @@ def main():
         for i in range(len(names)):
             stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
     set_profile_events(None)
+    ep_phases = None
+    if ep:
+        # the one-chunk step phase by phase, events on the compute stream
+        # (NCCL calls make it wait for their completion)
+        pnames = ["route", "pack", "count_exchange_host_sync", "rows_all_to_all", "expert_gemms",
+                  "partials_all_to_all", "shared_expert", "combine"]
+        pev = [torch.cuda.Event(enable_timing=True) for _ in range(len(pnames) + 1)]
+        ep_phases = dict.fromkeys(pnames, 0.0)
+        for _ in range(n_prof):
+            pev[0].record()
+            idx_, w_ = ep_layer.route(x)
+            pev[1].record()
+            counts_d, tok_rows, send_x, meta = ep_layer.pack(x, idx_, w_)
+            pev[2].record()
+            sc, rc = ep_layer.exchange.counts(counts_d)
+            pev[3].record()
+            recv_meta = ep_layer.exchange.rows(meta, sc, rc)
+            recv_x = ep_layer.exchange.rows(send_x, sc, rc)
+            pev[4].record()
+            part = ep_layer.compute(recv_x, recv_meta)
+            pev[5].record()
+            back = ep_layer.exchange.rows(part, rc, sc)
+            pev[6].record()
+            shared = ep_layer.shared_ffn(x)
+            pev[7].record()
+            ep_layer.combine(shared, back, tok_rows)
+            pev[8].record()
+            torch.cuda.synchronize()
+            for i, nme in enumerate(pnames):
+                ep_phases[nme] += pev[i].elapsed_time(pev[i + 1]) / n_prof
+        ep_phases["rows_per_rank_received"] = int(recv_x.shape[0])
+        ep_phases["rows_per_rank_sent"] = int(sum(sc))
     from dsmoe.ops import route as _route
     _gidx, _ = _route(x, store.get_gate_weight(LAYER), cfg,
                       score_bias=store.get_gate_bias(LAYER) if skew else None)
@@ -487,11 +527,14 @@ def main():
                        "router": cfg.router_mode, "baseline_config": args.config,
                        "hottest_expert_over_mean": hottest_over_mean,
                        "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
-                       "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU"},
+                       "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU",
+                       **({"ep_overlap": not args.no_overlap, "ep_chunks": args.chunks, "ep_sm_reserve": args.sm_reserve}
+                          if ep else {})},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},
             "roofline": roofline,
             "stages_ms": dict(zip(names, stage_ms)),
+            **({"ep_phases_ms": ep_phases} if ep_phases else {}),
             "layer": {"algorithmic_bytes": layer_bytes, "GB_s": layer_bytes / (layer_ms / 1e3) / 1e9,
                       "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm_peak,
                       "fp8_tflops_algorithmic": algo_flops / (ms_max / 1e3) / 1e12,

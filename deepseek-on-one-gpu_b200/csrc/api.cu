@@ -21,6 +21,10 @@ constexpr int kMaxProf = 8;
 thread_local cudaEvent_t g_prof[kMaxProf] = {};
 thread_local int g_nprof = 0;
 
+// Optional cap on the grouped GEMMs' persistent grid (dsmoe_set_gemm_sm_limit),
+// per host thread; 0 = one CTA per SM.
+thread_local int g_gemm_ctas = 0;
+
 void prof(int i, cudaStream_t s) {
   if (i < g_nprof && g_prof[i]) cudaEventRecord(g_prof[i], s);
 }
@@ -268,7 +272,8 @@ int run_gemm(const GemmJob& j, cudaStream_t s) {
   gp.sx = j.sx;
   gp.y = j.y;
   gp.status = j.status;
-  DSMOE_CUDA(launch_grouped_gemm(m_w0, m_w1, m_x, m_x32, gp, j.tile, num_sms(), s));
+  const int ctas = g_gemm_ctas > 0 && g_gemm_ctas < num_sms() ? g_gemm_ctas : num_sms();
+  DSMOE_CUDA(launch_grouped_gemm(m_w0, m_w1, m_x, m_x32, gp, j.tile, ctas, s));
   return DSMOE_OK;
 }
 
@@ -365,6 +370,12 @@ int dsmoe_set_profile_events(void* const* events, int32_t n) {
   if (n < 0 || n > kMaxProf || (n > 0 && !events)) return fail(DSMOE_ERR_INVALID, "0 <= n <= %d events", kMaxProf);
   for (int i = 0; i < kMaxProf; ++i) g_prof[i] = i < n ? static_cast<cudaEvent_t>(events[i]) : nullptr;
   g_nprof = n;
+  return DSMOE_OK;
+}
+
+int dsmoe_set_gemm_sm_limit(int32_t max_ctas) {
+  if (max_ctas < 0) return fail(DSMOE_ERR_INVALID, "max_ctas < 0");
+  g_gemm_ctas = max_ctas;
   return DSMOE_OK;
 }
 

@@ -23,7 +23,7 @@ EXPORTED = (
     "dsmoe_moe_experts", "dsmoe_expert_ffn_workspace_size", "dsmoe_fp8_linear_workspace_size",
     "dsmoe_expert_ffn", "dsmoe_fp8_linear", "dsmoe_read_status", "dsmoe_set_profile_events",
     "dsmoe_expert_ffn_noalloc", "dsmoe_ep_dispatch", "dsmoe_moe_local_workspace_size", "dsmoe_moe_local",
-    "dsmoe_ep_combine",
+    "dsmoe_ep_combine", "dsmoe_set_gemm_sm_limit",
 )
 
 
@@ -82,6 +82,7 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_moe_local_workspace_size.restype = sz
                 L.dsmoe_moe_local.argtypes = [cfgp, wp, vp, i32, vp, vp, vp, vp, sz, vp]
                 L.dsmoe_ep_combine.argtypes = [vp, vp, i32, i32, i32, vp, ctypes.c_float, vp, vp]
+                L.dsmoe_set_gemm_sm_limit.argtypes = [i32]
                 for name in EXPORTED:
                     getattr(L, name).restype = getattr(L, name).restype or ctypes.c_int
                 _lib = L
@@ -150,6 +151,13 @@ def moe_config(config) -> MoeConfig:
         router_mode=ROUTER_MODES[mode], norm_topk_prob=int(bool(config.norm_topk_prob)),
         routed_scaling_factor=float(config.routed_scaling_factor),
     )
+
+
+def set_gemm_sm_limit(max_ctas: int) -> None:
+    """Cap this thread's later grouped-GEMM launches at ``max_ctas`` CTAs (one
+    per SM; 0 = all SMs) so that a collective on another stream finds free
+    SMs."""
+    check(lib().dsmoe_set_gemm_sm_limit(int(max_ctas)), "dsmoe_set_gemm_sm_limit")
 
 
 def set_profile_events(events: list | None) -> None:

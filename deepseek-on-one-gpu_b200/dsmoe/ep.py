@@ -18,6 +18,19 @@ layer step (``EPLayer.forward``):
 The exchange is a small interface so the same step runs over
 ``torch.distributed`` (NCCL between GPUs, Gloo on CPU for the bookkeeping
 tests) or over an in-process emulation of W ranks on one GPU.
+
+Overlap (CUDA tensors, ``EPLayer.overlap``, the default): the count and row
+exchanges run on a side stream; the shared expert, which needs no exchange,
+is queued on the compute stream right after the packing, so it runs while
+the counts make their device->host trip and the rows travel. With
+``chunks=C`` > 1 the tokens are routed once and packed in C chunks under one
+count exchange; the expert GEMMs of a chunk then run while the next chunk's
+rows or the previous chunk's partials travel (each chunk re-reads the rank's
+expert weights, so this pays only where the exchange is long next to the
+GEMMs). While they overlap an exchange the grouped GEMMs leave ``sm_reserve``
+SMs free (``dsmoe_set_gemm_sm_limit``) so that the collective's kernels are
+not queued behind the persistent GEMM grid. Per token the arithmetic is the
+same in every mode.
 """
 from __future__ import annotations
 
@@ -48,11 +61,42 @@ class DistExchange:
         both = torch.cat([send_counts, recv]).tolist()
         return both[: self.world], both[self.world:]
 
+    def counts_chunks(self, counts_wc: torch.Tensor) -> tuple[list[list[int]], list[list[int]]]:
+        """One exchange for C chunks. ``counts_wc`` [W, C] int32: rows this
+        rank sends to rank d in chunk c. Returns per chunk the send splits
+        and the receive splits (by source rank)."""
+        W, C = counts_wc.shape
+        send = counts_wc.contiguous().reshape(-1)
+        recv = torch.empty_like(send)
+        self.dist.all_to_all_single(recv, send, group=self.group)
+        both = torch.cat([send, recv]).tolist()
+        s, r = both[: W * C], both[W * C:]
+        return ([[s[d * C + c] for d in range(W)] for c in range(C)],
+                [[r[q * C + c] for q in range(W)] for c in range(C)])
+
     def rows(self, send: torch.Tensor, send_splits: list[int], recv_splits: list[int]) -> torch.Tensor:
         out = send.new_empty((sum(recv_splits),) + tuple(send.shape[1:]))
         self.dist.all_to_all_single(out, send[: sum(send_splits)].contiguous(), output_split_sizes=recv_splits,
                                     input_split_sizes=send_splits, group=self.group)
         return out
+
+
+class LocalExchange:
+    """The exchange of a one-rank group: every row stays on the rank. Lets the
+    chunked, two-stream step run (and be tested) on a single GPU."""
+
+    world = 1
+
+    def counts(self, send_counts: torch.Tensor) -> tuple[list[int], list[int]]:
+        c = send_counts.tolist()
+        return c, c
+
+    def counts_chunks(self, counts_wc: torch.Tensor) -> tuple[list[list[int]], list[list[int]]]:
+        c = counts_wc.t().tolist()
+        return c, [list(x) for x in c]
+
+    def rows(self, send: torch.Tensor, send_splits: list[int], recv_splits: list[int]) -> torch.Tensor:
+        return send[: sum(send_splits)].clone()
 
 
 def local_config(config, world: int):
@@ -90,15 +134,27 @@ class EPLayer:
         self.bank.sync_table(non_blocking=False)
         self.shared = {p: (self.bank.w[p][0], self.bank.s[p][0]) for p in PROJS}
         self._ws = torch.zeros(0, dtype=torch.uint8, device=self.device)
+        self._comm = None  # side stream of the overlapped step
+        self.overlap = True  # CUDA tensors: exchange on a side stream, shared expert while rows travel
+        self.sm_reserve = 0  # SMs left to the collectives while GEMMs and all-to-alls overlap
 
     # -------------------------------------------------------------- phases
+    def route(self, x: torch.Tensor):
+        cfg = self.config
+        bias = self.store.get_gate_bias(self.layer) if getattr(cfg, "router_mode", "ref") == "v3" else None
+        return route(x, self.store.get_gate_weight(self.layer), cfg, score_bias=bias)
+
     def dispatch(self, x: torch.Tensor):
         """Route and pack. Returns (counts[W] int32 device, tok_rows, send_x, send_meta)."""
+        idx, w = self.route(x)
+        return self.pack(x, idx, w)
+
+    def pack(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor):
+        """Pack routed tokens for the exchange (``dsmoe_ep_dispatch``)."""
         cfg = self.config
         T, H = x.shape
         K = cfg.num_experts_per_tok
-        bias = self.store.get_gate_bias(self.layer) if getattr(cfg, "router_mode", "ref") == "v3" else None
-        idx, w = route(x, self.store.get_gate_weight(self.layer), cfg, score_bias=bias)
+        idx, w = idx.contiguous(), w.contiguous()
         cap = max(1, T * min(K, self.world))
         dev = x.device
         counts = torch.empty(self.world, dtype=torch.int32, device=dev)
@@ -138,20 +194,33 @@ class EPLayer:
                                     self._ws.numel(), stream_handle(recv_x.device)), "dsmoe_moe_local")
         return out
 
-    def finish(self, x: torch.Tensor, back: torch.Tensor, tok_rows: torch.Tensor) -> torch.Tensor:
-        """Shared expert on the rank's tokens + sum of the returned partials."""
-        T, H = x.shape
-        shared = expert_ffn(x, self.shared)
-        out = torch.empty_like(x)
+    def shared_ffn(self, x: torch.Tensor) -> torch.Tensor:
+        """The shared expert on the rank's own tokens (needs no exchange)."""
+        return expert_ffn(x, self.shared)
+
+    def combine(self, shared: torch.Tensor, back: torch.Tensor, tok_rows: torch.Tensor) -> torch.Tensor:
+        """``out = bf16(shared + bf16(scale * sum of the returned partials))``."""
+        T, H = shared.shape
+        out = torch.empty_like(shared)
         scale = 1.0 if getattr(self.config, "router_mode", "ref") == "v3" else float(self.config.routed_scaling_factor)
         check(lib().dsmoe_ep_combine(ptr(back) if back.numel() else None, ptr(tok_rows), T, self.world, H,
-                                     ptr(shared), scale, ptr(out), stream_handle(x.device)), "dsmoe_ep_combine")
+                                     ptr(shared), scale, ptr(out), stream_handle(shared.device)), "dsmoe_ep_combine")
         return out
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """One expert-parallel MoE step for this rank's tokens ``x`` [T, H] bf16."""
+    def finish(self, x: torch.Tensor, back: torch.Tensor, tok_rows: torch.Tensor) -> torch.Tensor:
+        """Shared expert on the rank's tokens + sum of the returned partials."""
+        return self.combine(self.shared_ffn(x), back, tok_rows)
+
+    def forward(self, x: torch.Tensor, chunks: int = 1) -> torch.Tensor:
+        """One expert-parallel MoE step for this rank's tokens ``x`` [T, H] bf16.
+        With ``overlap`` (default, CUDA tensors) the exchange runs on a side
+        stream while the shared expert runs; ``chunks`` > 1 also overlaps the
+        all-to-alls of one chunk with the expert GEMMs of another (each chunk
+        re-reads the rank's expert weights)."""
         shape = x.shape
         x = x.reshape(-1, shape[-1]).contiguous()
+        if self.overlap and x.is_cuda and x.shape[0] >= chunks:
+            return self._forward_overlapped(x, chunks).view(shape)
         counts, tok_rows, send_x, meta = self.dispatch(x)
         send_splits, recv_splits = self.exchange.counts(counts)
         recv_x = self.exchange.rows(send_x, send_splits, recv_splits)
@@ -159,6 +228,71 @@ class EPLayer:
         part = self.compute(recv_x, recv_meta)
         back = self.exchange.rows(part, recv_splits, send_splits)
         return self.finish(x, back, tok_rows).view(shape)
+
+
+    def _forward_overlapped(self, x: torch.Tensor, C: int) -> torch.Tensor:
+        T, H = x.shape
+        dev = x.device
+        cs = torch.cuda.current_stream(dev)
+        if self._comm is None:
+            self._comm = torch.cuda.Stream(device=dev)
+        comm = self._comm
+        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        limit = max(1, n_sm - self.sm_reserve) if self.sm_reserve > 0 else 0
+        bounds = [T * c // C for c in range(C + 1)]
+        idx, w = self.route(x)
+        packs = [self.pack(x[bounds[c]:bounds[c + 1]], idx[bounds[c]:bounds[c + 1]], w[bounds[c]:bounds[c + 1]])
+                 for c in range(C)]
+        counts_wc = torch.stack([p[0] for p in packs], dim=1)
+        packed = torch.cuda.Event()
+        packed.record(cs)
+        # The shared expert needs no exchange: it is queued first on the
+        # compute stream and runs while the counts and rows travel.
+        try:
+            _lib.set_gemm_sm_limit(limit)
+            shared = self.shared_ffn(x)
+        finally:
+            _lib.set_gemm_sm_limit(0)
+        comm.wait_event(packed)
+        arrived = []
+        with torch.cuda.stream(comm):
+            counts_wc.record_stream(comm)
+            send_sp, recv_sp = self.exchange.counts_chunks(counts_wc)  # the host waits for the side stream only
+            for c, (_, _, send_x, meta) in enumerate(packs):
+                send_x.record_stream(comm)
+                meta.record_stream(comm)
+                rx = self.exchange.rows(send_x, send_sp[c], recv_sp[c])
+                rm = self.exchange.rows(meta, send_sp[c], recv_sp[c])
+                rx.record_stream(cs)
+                rm.record_stream(cs)
+                ev = torch.cuda.Event()
+                ev.record(comm)
+                arrived.append((rx, rm, ev))
+        back = []
+        for c, (rx, rm, ev) in enumerate(arrived):
+            cs.wait_event(ev)
+            try:
+                # chunks before the last overlap the next chunk's traffic
+                _lib.set_gemm_sm_limit(limit if c < C - 1 else 0)
+                part = self.compute(rx, rm)
+            finally:
+                _lib.set_gemm_sm_limit(0)
+            done = torch.cuda.Event()
+            done.record(cs)
+            comm.wait_event(done)
+            with torch.cuda.stream(comm):
+                part.record_stream(comm)
+                b = self.exchange.rows(part, recv_sp[c], send_sp[c])
+                b.record_stream(cs)
+                ev_b = torch.cuda.Event()
+                ev_b.record(comm)
+            back.append((b, ev_b))
+        outs = []
+        for c, (b, ev_b) in enumerate(back):
+            cs.wait_event(ev_b)
+            t0, t1 = bounds[c], bounds[c + 1]
+            outs.append(self.combine(shared[t0:t1], b, packs[c][1]))
+        return outs[0] if C == 1 else torch.cat(outs)
 
 
 def emulate_step(layers: list[EPLayer], xs: list[torch.Tensor]) -> list[torch.Tensor]:

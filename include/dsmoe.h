@@ -151,6 +151,15 @@ DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_feature
 DSMOE_API int dsmoe_set_profile_events(void* const* events, int32_t n);
 
 /*
+ * Overlap hook (no reference counterpart; the reference has no collectives).
+ * Caps the persistent grid of the calling thread's later grouped-GEMM
+ * launches at max_ctas CTAs (one per SM), leaving the other SMs free for a
+ * collective running concurrently on another stream (the expert-parallel
+ * all-to-all). 0 (the default) uses every SM. Results do not depend on it.
+ */
+DSMOE_API int dsmoe_set_gemm_sm_limit(int32_t max_ctas);
+
+/*
  * Expert parallelism over W ranks (no counterpart in the reference, which is
  * single-GPU; SURVEY's EP row). Rank d owns routed experts
  * [d * experts_per_rank, (d+1) * experts_per_rank); gate and shared expert are

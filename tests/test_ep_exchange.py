@@ -1,5 +1,6 @@
 """The expert-parallel exchange (dsmoe.ep.DistExchange) on CPU with two Gloo
-ranks: count exchange, variable-split all-to-all there and back."""
+ranks: count exchange (one chunk and several), variable-split all-to-all
+there and back."""
 import os
 import socket
 
@@ -43,6 +44,12 @@ def _worker(rank, world, port, q):
                 off += 1
         back = ex.rows(recv * 2, rc, sc)  # the partial rows go back in the senders' order
         assert torch.equal(back, send[: sum(sc)] * 2)
+        # one count exchange for 3 chunks: rank r sends (10 r + 3 d + c) rows to d in chunk c
+        C = 3
+        cwc = torch.tensor([[10 * rank + 3 * d + c for c in range(C)] for d in range(world)], dtype=torch.int32)
+        scc, rcc = ex.counts_chunks(cwc)
+        assert scc == [[10 * rank + 3 * d + c for d in range(world)] for c in range(C)]
+        assert rcc == [[10 * s + 3 * rank + c for s in range(world)] for c in range(C)]
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))

@@ -68,3 +68,35 @@ def test_ep_rank_with_no_tokens_for_it():
     for r in range(W):
         single = moe_block(xs[r], 3, store, gt, cfg)
         assert O.rel_rms(outs[r].float().cpu(), single.float().cpu()) < 5e-3
+
+
+@pytest.mark.parametrize("chunks,reserve", [(1, 0), (1, 16), (2, 0), (3, 16), (5, 0)])
+def test_ep_overlapped_two_stream_step(chunks, reserve):
+    """The overlapped step (exchange on a side stream, shared expert while the
+    rows travel, optional chunking and SM reserve) on a one-rank group gives
+    the plain step's output and the single-GPU block's."""
+    from dsmoe.ep import LocalExchange
+
+    H, F = 512, 256
+    cfg = DeepSeekConfig(hidden_size=H, moe_intermediate_size=F)
+    store = SyntheticWeightStore(cfg, seed=71, device=DEV, pin_memory=False, gen_device="cpu")
+    layer = EPLayer(cfg, store, DEV, 2, 1, 0, exchange=LocalExchange(), expert_source=store.device_expert)
+    x = activations(72, 203, H).to(DEV)
+    layer.overlap = False
+    plain = layer.forward(x)
+    layer.overlap = True
+    layer.sm_reserve = reserve
+    ov = layer.forward(x, chunks=chunks)
+    again = layer.forward(x, chunks=chunks)
+    torch.cuda.synchronize()
+    assert torch.equal(ov, again)
+    assert O.rel_rms(ov.float().cpu(), plain.float().cpu()) < 1e-3
+    if chunks == 1:
+        assert torch.equal(ov, plain)
+    gt = GPUTransfer(cfg, store, DEV)
+    single = moe_block(x, 2, store, gt, cfg)
+    assert O.rel_rms(ov.float().cpu(), single.float().cpu()) < 5e-3
+    L = store.layer(2)
+    idx, w = O.route_ref(x.cpu(), L.gate)
+    ref = O.moe_block_grouped(x.cpu(), idx, w, L.expert, L.shared())
+    assert O.rel_rms(ov.float().cpu(), ref.float()) < REL_RMS_TOL

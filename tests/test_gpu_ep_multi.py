@@ -1,6 +1,7 @@
 """Expert parallelism across real GPUs (NCCL all-to-all): 2 ranks as
 processes, each rank's output compared with the single-GPU moe_block on the
-same tokens. Skipped when fewer than 2 GPUs are visible."""
+same tokens, for the one-chunk step and the chunked step that overlaps the
+all-to-alls with the GEMMs. Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -43,9 +44,12 @@ def _rank_main(rank, world, port, q):
         layer = EPLayer(cfg, store, dev, 3, world, rank, exchange=DistExchange(), expert_source=store.device_expert)
         gt = GPUTransfer(cfg, store, dev)
         results = []
-        for step, T in enumerate((64, 200, 1)):
+        steps = ((64, 1, 0, False), (200, 1, 0, False), (1, 1, 0, False), (64, 1, 0, True), (200, 1, 16, True),
+                 (1, 1, 0, True), (200, 3, 8, True), (64, 2, 0, True))
+        for step, (T, chunks, reserve, overlap) in enumerate(steps):
             x = activations(100 * step + rank, T, 512).to(dev)
-            out = layer.forward(x)
+            layer.overlap, layer.sm_reserve = overlap, reserve
+            out = layer.forward(x, chunks=chunks)
             single = moe_block(x, 3, store, gt, cfg)
             results.append(rel_rms(out.float().cpu(), single.float().cpu()))
         dist.barrier()
