@@ -20,6 +20,7 @@ With N > 1 every rank runs its own replica of the layer (weak scaling).
 from __future__ import annotations
 
 import argparse
+from datetime import datetime
 import csv
 import io
 import json
@@ -64,7 +65,7 @@ def peaks():
 class ClockSampler:
     """nvidia-smi sampling during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -75,12 +76,15 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
 
-    def stop(self):
+    def stop(self, window: tuple[float, float] | None = None):
+        """Median SM clock and the throttle reasons seen; with ``window``
+        (host time.time() bounds of the timed region) only samples inside it
+        count, if there are any."""
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -89,29 +93,26 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
             return None
-        sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for row in csv.reader(io.StringIO(out)):
-            if len(row) < 9:
+            if len(row) < 10:
                 continue
             try:
-                idx = int(row[0])
+                ts = datetime.strptime(row[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                idx = int(row[1])
+                rows.append((ts, idx, float(row[2]), float(row[3]),
+                             {n for n, v in zip(names, row[6:10]) if v.strip().lower() == "active"}))
             except ValueError:
                 continue
-            if idx not in self.gpus:
-                continue
-            try:
-                sm.append(float(row[1]))
-                mx.append(float(row[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, row[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        rows = [r for r in rows if r[1] in self.gpus]
+        inside = [r for r in rows if window and window[0] <= r[0] <= window[1]]
+        use = inside or rows
+        if not use:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(r[2] for r in use), "sm_max_mhz": max(r[3] for r in use),
+                "reasons": sorted(set().union(*(r[4] for r in use))), "samples": len(use),
+                "samples_in_timed_region": len(inside)}
 
 
 def cpu_sample(x_cpu, gate_cpu, get_expert, shared, budget_s: float, max_tokens: int):
@@ -212,6 +213,7 @@ def run_streaming(args, rank, world, local):
     sampler.start()
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_begin = time.time()
     e0.record()
     for i in range(steps):
         hd = h_host[args.warmup + i: args.warmup + i + 1].to(dev, non_blocking=True)  # the token in
@@ -219,7 +221,7 @@ def run_streaming(args, rank, world, local):
         out_host.copy_(h, non_blocking=True)  # its final hidden state out
     e1.record()
     torch.cuda.synchronize()
-    clocks = sampler.stop()
+    clocks = sampler.stop((t_begin, time.time()))
     ms = e0.elapsed_time(e1) / steps
     moved = dec.gt.bytes_h2d - b0
     misses, hits = dec.gt.slot_misses - m0, dec.gt.slot_hits - hit0
@@ -251,7 +253,7 @@ def run_streaming(args, rank, world, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="dsmoe", choices=["dsmoe", "reference"])
     ap.add_argument("--config", type=int, default=None, choices=[2, 3, 4, 5],
@@ -266,7 +268,7 @@ def main():
                     help="N > 1: expert-parallel over NCCL (default) or independent replicas")
     ap.add_argument("--chunks", type=int, default=1,
                     help="expert-parallel step: token chunks whose all-to-alls overlap the expert GEMMs (1 = none)")
-    ap.add_argument("--sm-reserve", type=int, default=16,
+    ap.add_argument("--sm-reserve", type=int, default=0,
                     help="expert-parallel step: SMs the grouped GEMMs leave to the all-to-alls while they overlap")
     ap.add_argument("--no-overlap", action="store_true",
                     help="expert-parallel step: exchange and GEMMs in one stream, one after the other")
@@ -351,14 +353,16 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_begin = time.time()
     e0.record()
     for _ in range(args.steps):
         step(x)
     e1.record()
     torch.cuda.synchronize()
+    t_end = time.time()
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop() if rank == 0 else None
+    clocks = sampler.stop((t_begin, t_end)) if rank == 0 else None
     ms = e0.elapsed_time(e1) / args.steps
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -373,7 +377,7 @@ def main():
     if ep:
         names[1] = "dispatch+all_to_all+permute"
     stage_ms = [0.0] * len(names)
-    n_prof = max(3, args.steps // 2)
+    n_prof = min(20, max(3, args.steps // 2))
     for _ in range(n_prof):
         if ep:
             # stage events come from the route and the rank's expert GEMMs; the

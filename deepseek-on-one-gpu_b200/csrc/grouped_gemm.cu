@@ -79,7 +79,9 @@ struct Cfg {
   static constexpr int NUM_BARS = 2 * STAGES + 2 * NBUF + 1;
   static constexpr int MISC_OFF = BAR_OFF + 8 * NUM_BARS;
   static constexpr int TABLE_OFF = ((MISC_OFF + 16 + 15) / 16) * 16;
-  static constexpr int SMEM_BYTES = TABLE_OFF + 4 * 4 * MAX_GROUPS + 1024;  // + alignment slack
+  // the per-group tables stay in global memory (L1-cached): shared memory
+  // goes to the stage ring
+  static constexpr int SMEM_BYTES = TABLE_OFF + 1024;  // + alignment slack
   static_assert(BN % 32 == 0 && BN <= 256 && EPI_COLS % CHUNK == 0 && NBUF * TCOLS <= 512 &&
                     (!NCAT || 2 * BN <= 256), "tile shape");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
@@ -122,23 +124,15 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   uint64_t* done_bar = tempty + NBUF;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
-  int* s_ustart = reinterpret_cast<int*>(smem + C::TABLE_OFF);
-  int* s_counts = s_ustart + MAX_GROUPS;
-  int* s_rows = s_counts + MAX_GROUPS;
-  int* s_slot = s_rows + MAX_GROUPS;
+  const int* __restrict__ s_ustart = p.unit_start;
+  const int* __restrict__ s_counts = p.counts;
+  const int* __restrict__ s_rows = p.row_start;
+  const int* __restrict__ s_slot = p.slot_of;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int NG = p.n_groups;
 
-  for (int i = threadIdx.x; i <= NG; i += blockDim.x) {
-    s_ustart[i] = p.unit_start[i];
-    if (i < NG) {
-      s_counts[i] = p.counts[i];
-      s_rows[i] = p.row_start[i];
-      s_slot[i] = p.slot_of[i];
-    }
-  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -395,7 +389,7 @@ cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, co
     case 32: return gg::launch_cfg<32, 8, 8, true>(w0, w1, x, x32, p, grid, stream);
     case 64: return gg::launch_cfg<64, 6, 4, true>(w0, w1, x, x32, p, grid, stream);
     case 128: return gg::launch_cfg<128, 4, 2, true>(w0, w1, x, x32, p, grid, stream);
-    case 160: return gg::launch_cfg<160, 3, 3, false>(w0, w1, x, x32, p, grid, stream);
+    case 160: return gg::launch_cfg<160, 4, 3, false>(w0, w1, x, x32, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
