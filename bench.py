@@ -45,7 +45,7 @@ FP8_DENSE_NOMINAL_TFLOPS = 4500.0
 # one token tile) measured by ncu on a 33-expert, T=512 launch of the same
 # kernel: 1.109 GB over 1,152 units. The full-size launch is too large for a
 # multi-pass ncu capture, so its traffic is this figure times its units.
-GATEUP_DRAM_BYTES_PER_UNIT = 1.109e9 / 1152
+GATEUP_DRAM_BYTES_PER_UNIT = 1.0947e9 / 1152  # ncu DRAM bytes of the 33-expert T=512 gate/up capture per work unit
 
 
 def gemm_tile(tokens: int) -> int:
