@@ -472,26 +472,89 @@ def main():
     # ------------------------------------------------------------------ e2e
     if args.skip_e2e:
         args.steps_e2e = 0
+    # A stream of batches through the public call, as a serving loop runs it:
+    # every step copies its input from pinned host memory and reads its output
+    # back; the copies run on two copy streams (one per direction) with two
+    # device input buffers, so step i+1's input and step i-1's output move
+    # while step i computes. The timed region runs from the first input copy
+    # to the last output copy.
     x_host = x.cpu().pin_memory()
-    out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    x_in = torch.empty_like(x)
-    for _ in range(0 if args.skip_e2e else 3):
-        x_in.copy_(x_host, non_blocking=True)
-        out_host.copy_(step(x_in), non_blocking=True)
+    outs_host = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    x_in = [torch.empty_like(x) for _ in range(2)]
+    cs = torch.cuda.current_stream(dev)
+    h2d, d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_run(n, start=None, end=None):
+        if start is not None:
+            start.record(h2d)
+        with torch.cuda.stream(h2d):
+            x_in[0].copy_(x_host, non_blocking=True)
+        in_ready[0].record(h2d)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                nb = (i + 1) % 2
+                if i >= 1:
+                    h2d.wait_event(computed[nb])  # step i-1 is done with that buffer
+                with torch.cuda.stream(h2d):
+                    x_in[nb].copy_(x_host, non_blocking=True)
+                in_ready[nb].record(h2d)
+            cs.wait_event(in_ready[b])
+            y = step(x_in[b])
+            computed[b].record(cs)
+            d2h.wait_event(computed[b])
+            with torch.cuda.stream(d2h):
+                y.record_stream(d2h)
+                outs_host[b].copy_(y, non_blocking=True)
+        if end is not None:
+            end.record(d2h)
+
+    if not args.skip_e2e:
+        e2e_run(3)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record()
-    for _ in range(1 if args.skip_e2e else args.steps):
-        x_in.copy_(x_host, non_blocking=True)
-        out_host.copy_(step(x_in), non_blocking=True)
-    e3.record()
+    n_e2e = 1 if args.skip_e2e else args.steps
+    e2e_run(n_e2e, e2, e3)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e2.elapsed_time(e3) / (1 if args.skip_e2e else args.steps)], device=dev)
+    e2e_ms = torch.tensor([e2.elapsed_time(e3) / n_e2e], device=dev)
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = world * T / (float(e2e_ms.item()) / 1000.0)
+    # ------------------------------------ widened rows (1 GPU, same layer)
+    # The MoE layer's FFN half (norm + block + residual in one library call),
+    # RMSNorm alone, and the dense FFN of layers 0-2 (intermediate 18432)
+    # through the same FP8 GEMM, on this batch. Device-timed.
+    widened = None
+    if world == 1 and not ep:
+        from dsmoe import dense_ffn, moe_layer_ffn, rms_norm
+        from dsmoe.synthetic import expert_weights
+
+        def dev_ms(fn, n=10):
+            for _ in range(3):
+                fn()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / n
+
+        ln = store.get_layer_norm_weights(LAYER)[1]
+        norm_ms = dev_ms(lambda: rms_norm(x, ln, cfg.rms_norm_eps))
+        ffn_ms = dev_ms(lambda: moe_layer_ffn(x, LAYER, store, gt, cfg))
+        dense_w = {p: (w.to(dev), s.to(dev)) for p, (w, s) in expert_weights(5, 0, 0, H, 18432, "cuda").items()}
+        dn_ms = dev_ms(lambda: dense_ffn(x, dense_w))
+        dense_bytes = 3 * 18432 * H + T * H * 2 * 2
+        widened = {"rms_norm_ms": norm_ms, "rms_norm_GB_s": 2 * T * H * 2 / (norm_ms / 1e3) / 1e9,
+                   "moe_layer_ffn_ms": ffn_ms, "moe_layer_ffn_over_block": ffn_ms / ms_max,
+                   "dense_ffn_ms": dn_ms, "dense_ffn_tflops": 2.0 * T * 3 * 18432 * H / (dn_ms / 1e3) / 1e12,
+                   "dense_ffn_weight_GB": dense_bytes / 1e9}
+        del dense_w
     status = Workspace.get(dev).status()
 
     # ---------------------------------------------------------- CPU oracle
@@ -535,7 +598,9 @@ def main():
                        **({"ep_overlap": not args.no_overlap, "ep_chunks": args.chunks, "ep_sm_reserve": args.sm_reserve}
                           if ep else {})},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
-                    "d2h_bytes_per_step": T * H * 2},
+                    "d2h_bytes_per_step": T * H * 2,
+                    "copies": "pinned host buffers; H2D and D2H on their own streams, double-buffered, "
+                              "overlapping the neighbouring steps' compute"},
             "roofline": roofline,
             "stages_ms": dict(zip(names, stage_ms)),
             **({"ep_phases_ms": ep_phases} if ep_phases else {}),
@@ -544,6 +609,7 @@ def main():
                       "fp8_tflops_algorithmic": algo_flops / (ms_max / 1e3) / 1e12,
                       "fp8_frac_of_nominal_dense": algo_flops / (ms_max / 1e3) / 1e12 / FP8_DENSE_NOMINAL_TFLOPS,
                       "experts_touched": touched},
+            **({"widened_rows": widened} if widened else {}),
             "gpu_launches": 9 * args.steps,
             "device_status": status,
             "clocks": clocks,

@@ -47,6 +47,9 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 
 constexpr size_t kAlign = 256;
+// Feature sizes of the single-matrix entry points (dsmoe_expert_ffn,
+// dsmoe_fp8_linear): the dense FFN layers need 18432; row offsets stay in int.
+constexpr int kMaxFeatures = 32768;
 size_t align_up(size_t v, size_t a = kAlign) { return (v + a - 1) / a * a; }
 int round32(int v) { return (v + 31) & ~31; }
 
@@ -323,7 +326,7 @@ int run_ffn(const void* w_gate, const float* s_gate, const void* w_up, const flo
 
 // Permute + both grouped GEMMs + combine, routing already in the workspace.
 int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, const void* hidden, int T, void* out,
-               const Ws& L, void* ws, cudaStream_t s) {
+               const Ws& L, void* ws, cudaStream_t s, const void* residual = nullptr) {
   const int H = c->hidden, F = c->inter, K = c->top_k, NG = L.NG;
   int32_t* counts = at<int32_t>(ws, L.counts);
   int32_t* row_start = at<int32_t>(ws, L.row_start);
@@ -347,7 +350,7 @@ int do_experts(const dsmoe_moe_config_t* c, const dsmoe_layer_weights_t* wt, con
 
   const float scale = c->router_mode == DSMOE_ROUTER_V3 ? 1.0f : c->routed_scaling_factor;
   DSMOE_CUDA(launch_combine(y, T, H, pos, at<float>(ws, L.w), K, row_start, scale, 1,
-                            static_cast<__nv_bfloat16*>(out), s));
+                            static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), s));
   prof(6, s);
   return DSMOE_OK;
 }
@@ -431,6 +434,46 @@ int dsmoe_moe_forward(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t
   return do_experts(cfg, w, hidden, tokens, out, L, workspace, s);
 }
 
+int dsmoe_rms_norm(const void* x, const void* weight, float eps, int32_t tokens, int32_t hidden, void* out,
+                   dsmoe_stream_t stream) {
+  if (tokens < 0 || hidden <= 0 || hidden % 8) return fail(DSMOE_ERR_INVALID, "tokens >= 0, hidden > 0 and % 8 == 0");
+  if (!(eps >= 0.f)) return fail(DSMOE_ERR_INVALID, "eps must be >= 0");
+  if (tokens == 0) return DSMOE_OK;
+  if (!x || !weight || !out || !aligned16(x) || !aligned16(weight) || !aligned16(out))
+    return fail(DSMOE_ERR_INVALID, "x / weight / out NULL or not 16-byte aligned");
+  DSMOE_CUDA(launch_rmsnorm(x, weight, eps, tokens, hidden, out, reinterpret_cast<cudaStream_t>(stream)));
+  return DSMOE_OK;
+}
+
+size_t dsmoe_moe_layer_ffn_workspace_size(const dsmoe_moe_config_t* cfg, int32_t tokens) {
+  if (check_cfg(cfg) != DSMOE_OK || tokens < 0) return 0;
+  const size_t moe = plan_moe(tokens, cfg->hidden, cfg->inter, cfg->n_routed, cfg->top_k).total;
+  return moe + ((static_cast<size_t>(tokens) * cfg->hidden * 2 + 255) & ~size_t(255));
+}
+
+int dsmoe_moe_layer_ffn(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden,
+                        const void* norm_weight, float eps, int32_t tokens, void* out, int64_t* topk_idx,
+                        float* topk_w, void* workspace, size_t workspace_bytes, dsmoe_stream_t stream) {
+  int r = check_cfg(cfg);
+  if (r) return r;
+  if ((r = check_weights(cfg, w))) return r;
+  if (tokens < 0) return fail(DSMOE_ERR_INVALID, "tokens < 0");
+  if (!(eps >= 0.f)) return fail(DSMOE_ERR_INVALID, "eps must be >= 0");
+  if (tokens == 0) return DSMOE_OK;
+  if (!hidden || !out || !norm_weight || !aligned16(hidden) || !aligned16(out) || !aligned16(norm_weight))
+    return fail(DSMOE_ERR_INVALID, "hidden / norm_weight / out NULL or not 16-byte aligned");
+  if (out == hidden) return fail(DSMOE_ERR_INVALID, "out must not alias hidden");
+  const Ws L = plan_moe(tokens, cfg->hidden, cfg->inter, cfg->n_routed, cfg->top_k);
+  const size_t need = dsmoe_moe_layer_ffn_workspace_size(cfg, tokens);
+  if (!workspace || workspace_bytes < need)
+    return fail(DSMOE_ERR_WORKSPACE, "workspace %zu bytes, need %zu", workspace_bytes, need);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  void* normed = static_cast<uint8_t*>(workspace) + L.total;  // L.total is a multiple of the 256-byte alignment
+  DSMOE_CUDA(launch_rmsnorm(hidden, norm_weight, eps, tokens, cfg->hidden, normed, s));
+  if ((r = do_route(cfg, normed, w->gate_weight, w->score_bias, tokens, topk_idx, topk_w, L, workspace, s))) return r;
+  return do_experts(cfg, w, normed, tokens, out, L, workspace, s, hidden);
+}
+
 size_t dsmoe_expert_ffn_workspace_size(int32_t tokens, int32_t hidden, int32_t inter) {
   if (tokens < 0 || hidden <= 0 || inter <= 0) return 0;
   return plan_single(tokens, hidden, inter).total;
@@ -457,8 +500,9 @@ int dsmoe_expert_ffn(const void* x, int32_t tokens, int32_t hidden, int32_t inte
                      const float* s_gate, const void* w_up, const float* s_up, const void* w_down,
                      const float* s_down, void* out, void* workspace, size_t workspace_bytes,
                      dsmoe_stream_t stream) {
-  if (hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128 || hidden > 8192 || inter > 8192)
-    return fail(DSMOE_ERR_UNSUPPORTED, "hidden (%d) / inter (%d) must be multiples of 128 up to 8192", hidden, inter);
+  if (hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128 || hidden > kMaxFeatures || inter > kMaxFeatures)
+    return fail(DSMOE_ERR_UNSUPPORTED, "hidden (%d) / inter (%d) must be multiples of 128 up to %d", hidden, inter,
+                kMaxFeatures);
   if (tokens < 0) return fail(DSMOE_ERR_INVALID, "tokens < 0");
   if (tokens == 0) return DSMOE_OK;
   const void* ps[9] = {x, w_gate, s_gate, w_up, s_up, w_down, s_down, out, workspace};
@@ -479,9 +523,11 @@ int dsmoe_expert_ffn(const void* x, int32_t tokens, int32_t hidden, int32_t inte
 int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_features, int32_t out_features, const void* weight,
                      const float* scale_inv, void* out, void* workspace, size_t workspace_bytes,
                      dsmoe_stream_t stream) {
-  if (in_features <= 0 || in_features % 128 || out_features <= 0 || out_features % 128 || in_features > 8192)
-    return fail(DSMOE_ERR_UNSUPPORTED, "in (%d) / out (%d) features must be multiples of 128 (in <= 8192)",
-                in_features, out_features);
+  if (in_features <= 0 || in_features % 128 || out_features <= 0 || out_features % 8 ||
+      in_features > kMaxFeatures || out_features > kMaxFeatures)
+    return fail(DSMOE_ERR_UNSUPPORTED,
+                "in (%d) features must be a multiple of 128 and out (%d) of 8, both up to %d", in_features,
+                out_features, kMaxFeatures);
   if (tokens < 0) return fail(DSMOE_ERR_INVALID, "tokens < 0");
   if (tokens == 0) return DSMOE_OK;
   const void* ps[5] = {x, weight, scale_inv, out, workspace};
@@ -492,7 +538,7 @@ int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_features, int32_t
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int r;
   int32_t* counts = at<int32_t>(workspace, L.counts);
-  if ((r = single_prologue(x, tokens, in_features, 0, out_features / 128, L, workspace, s))) return r;
+  if ((r = single_prologue(x, tokens, in_features, 0, (out_features + 127) / 128, L, workspace, s))) return r;
   GemmJob j{};
   j.w0 = j.w1 = weight;
   j.s0 = j.s1 = scale_inv;
@@ -571,7 +617,7 @@ int dsmoe_moe_local(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* 
   if ((r = run_ffn(w->w_gate, w->s_gate, w->w_up, w->s_up, w->w_down, w->s_down, w->n_slots, H, F, L, ws,
                    w->slot_of_expert, NG, y, s)))
     return r;
-  DSMOE_CUDA(launch_combine(y, rows, H, pos, local_w, K, row_start, 1.0f, 0,
+  DSMOE_CUDA(launch_combine(y, rows, H, pos, local_w, K, row_start, 1.0f, 0, nullptr,
                             static_cast<__nv_bfloat16*>(partial_out), s));
   prof(6, s);
   return DSMOE_OK;

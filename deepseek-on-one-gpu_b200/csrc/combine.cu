@@ -7,6 +7,8 @@
 //   out[t] = bf16(y_shared[t] + bf16(acc * scale))
 // Without a shared expert (a rank's share of an expert-parallel step) the
 // output is bf16(acc): the rank's partial, summed and scaled by the caller.
+// With a residual r (the MoE layer's FFN half, inference/forward.py:109) the
+// output is bf16(r[t] + out[t]): the layer's `hidden + ffn_out` in bf16.
 // This is the reference's arithmetic (inference/forward.py:137,151,153): the
 // fp32 0-dim weight times a bf16 row yields bf16 (the weight is rounded to
 // bf16 by type promotion), the running sum is bf16 and accumulates in top-k
@@ -21,7 +23,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
                                                       const int32_t* __restrict__ pos,
                                                       const float* __restrict__ w, int top_k,
                                                       const int32_t* __restrict__ row_start, float scale,
-                                                      int has_shared, __nv_bfloat16* __restrict__ out) {
+                                                      int has_shared, const __nv_bfloat16* __restrict__ residual,
+                                                      __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
   __shared__ int s_row[8];
   __shared__ float s_w[8];
@@ -65,16 +68,22 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 #pragma unroll
       for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(acc[i]);
     }
+    if (residual) {
+      const uint4 rv = __ldg(reinterpret_cast<const uint4*>(residual + static_cast<size_t>(t) * H) + c);
+      const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__bfloat162float(rb[i]) + __bfloat162float(ob[i]));
+    }
     reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H)[c] = o;
   }
 }
 }  // namespace cb
 
 cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
-                           const int32_t* row_start, float scale, int has_shared, __nv_bfloat16* out,
-                           cudaStream_t stream) {
+                           const int32_t* row_start, float scale, int has_shared, const __nv_bfloat16* residual,
+                           __nv_bfloat16* out, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  cb::combine_kernel<<<T, 256, 0, stream>>>(y, T, H, pos, w, top_k, row_start, scale, has_shared, out);
+  cb::combine_kernel<<<T, 256, 0, stream>>>(y, T, H, pos, w, top_k, row_start, scale, has_shared, residual, out);
   return cudaGetLastError();
 }
 

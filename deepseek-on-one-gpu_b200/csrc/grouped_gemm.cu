@@ -160,7 +160,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   const uint32_t tmem_base = *s_tmem;
   const int total_units = s_ustart[NG];
   const int n_kb = p.K / BK;
-  const int mt_per_mat = p.M / BM;
+  // 128-row tiles per matrix; a ragged last tile (single-slot linear layers
+  // such as 576 outputs) reads zero-filled rows past the end of the weight
+  // and stores only rows < M.
+  const int mt_per_mat = (p.M + BM - 1) / BM;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -286,17 +289,20 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       const int ncols = min(BN, s_counts[g] - nt * BN);
       const int nvalid = max(0, min(EPI_COLS, ncols - c0));  // valid columns of this warp
       const int mat = mt >= mt_per_mat;
-      // Weight block scales of this unit's 128-row tile, one per K block:
-      // lane i holds kb = i and kb = 32 + i.
-      float swr0, swr1;
-      {
-        const bool slot_ok = slot >= 0 && slot < p.n_slots;  // the producer reports a bad slot
-        const float* ws = mat ? p.wscale1 : p.wscale0;
-        const size_t base =
-            (static_cast<size_t>(slot_ok ? slot : 0) * mt_per_mat + (mt - mat * mt_per_mat)) * n_kb;
-        swr0 = slot_ok && lane < n_kb ? __ldg(ws + base + lane) : 0.f;
-        swr1 = slot_ok && 32 + lane < n_kb ? __ldg(ws + base + 32 + lane) : 0.f;
-      }
+      // Weight block scales of this unit's 128-row tile, one per K block, in
+      // two 32-block windows: lane i holds kb = 32w + i of window w in
+      // register w % 2; entering window w refills the other register with
+      // window w + 1, 32 K steps before it is needed.
+      const bool slot_ok = slot >= 0 && slot < p.n_slots;  // the producer reports a bad slot
+      const float* wsc = (mat ? p.wscale1 : p.wscale0) +
+                         (static_cast<size_t>(slot_ok ? slot : 0) * mt_per_mat + (mt - mat * mt_per_mat)) * n_kb;
+      float swr0 = slot_ok && lane < n_kb ? __ldg(wsc + lane) : 0.f;
+      float swr1 = slot_ok && 32 + lane < n_kb ? __ldg(wsc + 32 + lane) : 0.f;
+      // Per-row activation scales of this warp's columns (lane i holds column
+      // i and 32 + i), loaded now so that the latency hides behind the K loop.
+      const int row_base = s_rows[g] + nt * BN + c0;
+      const float sxa = lane < nvalid ? __ldg(p.sx + row_base + lane) : 0.f;
+      const float sxb = 32 + lane < nvalid ? __ldg(p.sx + row_base + 32 + lane) : 0.f;
       float acc[EPI_COLS];
 #pragma unroll
       for (int i = 0; i < EPI_COLS; ++i) acc[i] = 0.f;
@@ -304,7 +310,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       for (int kb = 0; kb < n_kb; ++kb) {
         if (!mbar_wait(&tfull[tb], tphase, p.status, kDevTimeoutEpilogue, s_abort)) { ok = false; break; }
         tc_fence_after();
-        const float sw = __shfl_sync(0xffffffffu, kb < 32 ? swr0 : swr1, kb & 31);
+        if ((kb & 31) == 0 && kb >= 32) {
+          const int nk = kb + 32 + lane;
+          const float v = slot_ok && nk < n_kb ? __ldg(wsc + nk) : 0.f;
+          if ((kb >> 5) & 1) swr0 = v; else swr1 = v;
+        }
+        const float sw = __shfl_sync(0xffffffffu, ((kb >> 5) & 1) ? swr1 : swr0, kb & 31);
 #pragma unroll
         for (int q = 0; q < EPI_COLS / CHUNK; ++q) {
           if (q * CHUNK < nvalid) {  // warp-uniform
@@ -332,16 +343,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         if (++tb == NBUF) { tb = 0; tphase ^= 1; }
       }
       if (!ok) break;
-      const int row_base = s_rows[g] + nt * BN + c0;
-      const int feat = mt * BM + quad * 32 + lane;
-      // Per-row activation scales of this warp's columns, lane i holds column
-      // i and 32 + i.
-      const float sxa = lane < nvalid ? __ldg(p.sx + row_base + lane) : 0.f;
-      const float sxb = 32 + lane < nvalid ? __ldg(p.sx + row_base + 32 + lane) : 0.f;
+      const int row_in_mat = (mt - mat * mt_per_mat) * BM + quad * 32 + lane;
+      const int feat = mat * p.M + row_in_mat;
+      const bool row_ok = row_in_mat < p.M;
 #pragma unroll
       for (int i = 0; i < EPI_COLS; ++i) {
         const float s = __shfl_sync(0xffffffffu, i < 32 ? sxa : sxb, i & 31);
-        if (i < nvalid) p.y[static_cast<size_t>(row_base + i) * out_ld + feat] = __float2bfloat16_rn(acc[i] * s);
+        if (i < nvalid && row_ok)
+          p.y[static_cast<size_t>(row_base + i) * out_ld + feat] = __float2bfloat16_rn(acc[i] * s);
       }
     }
   }
@@ -383,7 +392,7 @@ int gemm_tile_tokens(int tokens) {
 
 cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                                 const CUtensorMap& x32, const GemmParams& p, int tile, int grid, cudaStream_t stream) {
-  if (p.n_groups > gg::MAX_GROUPS - 1 || p.K / gg::BK > 64 || (p.n_mat != 1 && p.n_mat != 2))
+  if (p.n_groups > gg::MAX_GROUPS - 1 || (p.n_mat != 1 && p.n_mat != 2))
     return cudaErrorInvalidValue;
   switch (tile) {
     case 32: return gg::launch_cfg<32, 8, 8, true>(w0, w1, x, x32, p, grid, stream);

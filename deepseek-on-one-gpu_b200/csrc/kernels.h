@@ -60,9 +60,13 @@ cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx
                                  float* sx, int32_t* pos, cudaStream_t stream);
 
 // Combine (combine.cu)
+// residual (optional, [T][H]): out = bf16(residual + combined row)
 cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
-                           const int32_t* row_start, float scale, int has_shared, __nv_bfloat16* out,
-                           cudaStream_t stream);
+                           const int32_t* row_start, float scale, int has_shared, const __nv_bfloat16* residual,
+                           __nv_bfloat16* out, cudaStream_t stream);
+
+// y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), one row of H per token
+cudaError_t launch_rmsnorm(const void* x, const void* w, float eps, int T, int H, void* y, cudaStream_t stream);
 
 // Expert parallelism (ep.cu)
 cudaError_t launch_ep_dispatch(const int64_t* idx, const float* w, const void* x, int T, int K, int H, int W, int El,

@@ -1,17 +1,18 @@
 """dsmoe — B200-native (sm_100a) DeepSeek-R1 MoE block.
 
 Drop-in for the MoE hot path of sushruta/deepseek-on-one-gpu: ``route``,
-``fp8_linear``, ``expert_ffn`` (``inference/ops.py``), ``moe_block``
+``fp8_linear``, ``expert_ffn``, ``rms_norm`` (``inference/ops.py``),
+``moe_block`` and the MoE layer's FFN half ``moe_layer_ffn``
 (``inference/forward.py``), ``GPUTransfer`` (``inference/gpu_transfer.py``) and
 ``ExpertCache`` (``inference/weight_store.py``), all backed by ``libdsmoe.so``.
 """
 from .config import DeepSeekConfig, load_config
-from .forward import moe_block
+from .forward import moe_block, moe_layer_ffn
 from .gpu_transfer import GPUTransfer, LayerBank
-from .ops import expert_ffn, fp8_linear, route, swiglu
+from .ops import dense_ffn, expert_ffn, fp8_linear, rms_norm, route, swiglu
 from .weight_store import ExpertCache, SyntheticWeightStore
 
 __all__ = [
-    "DeepSeekConfig", "load_config", "moe_block", "GPUTransfer", "LayerBank", "expert_ffn", "fp8_linear",
-    "route", "swiglu", "ExpertCache", "SyntheticWeightStore",
+    "DeepSeekConfig", "load_config", "moe_block", "moe_layer_ffn", "GPUTransfer", "LayerBank", "dense_ffn",
+    "expert_ffn", "fp8_linear", "rms_norm", "route", "swiglu", "ExpertCache", "SyntheticWeightStore",
 ]

@@ -23,7 +23,8 @@ EXPORTED = (
     "dsmoe_moe_experts", "dsmoe_expert_ffn_workspace_size", "dsmoe_fp8_linear_workspace_size",
     "dsmoe_expert_ffn", "dsmoe_fp8_linear", "dsmoe_read_status", "dsmoe_set_profile_events",
     "dsmoe_expert_ffn_noalloc", "dsmoe_ep_dispatch", "dsmoe_moe_local_workspace_size", "dsmoe_moe_local",
-    "dsmoe_ep_combine", "dsmoe_set_gemm_sm_limit",
+    "dsmoe_ep_combine", "dsmoe_set_gemm_sm_limit", "dsmoe_rms_norm", "dsmoe_moe_layer_ffn_workspace_size",
+    "dsmoe_moe_layer_ffn",
 )
 
 
@@ -83,6 +84,10 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_moe_local.argtypes = [cfgp, wp, vp, i32, vp, vp, vp, vp, sz, vp]
                 L.dsmoe_ep_combine.argtypes = [vp, vp, i32, i32, i32, vp, ctypes.c_float, vp, vp]
                 L.dsmoe_set_gemm_sm_limit.argtypes = [i32]
+                L.dsmoe_rms_norm.argtypes = [vp, vp, ctypes.c_float, i32, i32, vp, vp]
+                L.dsmoe_moe_layer_ffn_workspace_size.argtypes = [cfgp, i32]
+                L.dsmoe_moe_layer_ffn_workspace_size.restype = sz
+                L.dsmoe_moe_layer_ffn.argtypes = [cfgp, wp, vp, vp, ctypes.c_float, i32, vp, vp, vp, vp, sz, vp]
                 for name in EXPORTED:
                     getattr(L, name).restype = getattr(L, name).restype or ctypes.c_int
                 _lib = L

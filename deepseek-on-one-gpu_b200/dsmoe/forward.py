@@ -75,3 +75,39 @@ def moe_block(hidden: torch.Tensor, layer_idx: int, weight_store, gpu_transfer, 
         shape = tuple(hidden.shape[:-1]) + (K,)
         return out, idx.view(shape), w.view(shape)
     return out
+
+
+def moe_layer_ffn(hidden: torch.Tensor, layer_idx: int, weight_store, gpu_transfer, config,
+                  verbose: bool = False) -> torch.Tensor:
+    """The FFN half of a MoE transformer layer (``inference/forward.py:97-109``
+    for ``layer_idx >= first_k_dense_replace``):
+    ``hidden + moe_block(rms_norm(hidden, post_attention_layernorm))``, bf16.
+    With every expert of the layer resident this is one library call
+    (``dsmoe_moe_layer_ffn``: the norm kernel, the MoE kernels, and the
+    residual add inside the combine)."""
+    H = hidden.shape[-1]
+    x = hidden.reshape(-1, H).contiguous()
+    if x.dtype != torch.bfloat16:
+        raise TypeError("moe_layer_ffn expects bf16 hidden states")
+    _, post_ln = weight_store.get_layer_norm_weights(layer_idx)
+    eps = float(getattr(config, "rms_norm_eps", 1e-6))
+    bank = gpu_transfer.bank(layer_idx)
+    if not bank.fully_resident:
+        from .ops import rms_norm
+        normed = rms_norm(x, post_ln, eps)
+        return (x + moe_block(normed, layer_idx, weight_store, gpu_transfer, config, verbose=verbose)).view(
+            hidden.shape)
+    gate_weight = weight_store.get_gate_weight(layer_idx)
+    bias = weight_store.get_gate_bias(layer_idx) if getattr(config, "router_mode", "ref") == "v3" else None
+    require_cuda(x, gate_weight, bias, post_ln)
+    cfg = _lib.moe_config(config)
+    T, K = x.shape[0], cfg.top_k
+    out = torch.empty_like(x)
+    idx = torch.empty(T, K, dtype=torch.int64, device=x.device)
+    w = torch.empty(T, K, dtype=torch.float32, device=x.device)
+    ws = _lib.Workspace.get(x.device).ensure(lib().dsmoe_moe_layer_ffn_workspace_size(cfg, T))
+    lw = _layer_weights(bank, gate_weight, bias)
+    check(lib().dsmoe_moe_layer_ffn(cfg, lw, ptr(x), ptr(post_ln), eps, T, ptr(out), ptr(idx), ptr(w), ptr(ws),
+                                    ws.numel(), stream_handle(x.device)), "dsmoe_moe_layer_ffn")
+    gpu_transfer.mark_used(layer_idx)
+    return out.view(hidden.shape)

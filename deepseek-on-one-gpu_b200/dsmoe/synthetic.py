@@ -105,6 +105,13 @@ def score_bias(seed: int, layer: int, n_experts: int, device="cpu", std: float =
     return b.to(device)
 
 
+def norm_weight(seed: int, layer: int, which: int, hidden: int, device="cpu", std: float = 0.1) -> torch.Tensor:
+    """A layer-norm weight (``which`` 0 = input_layernorm, 1 =
+    post_attention_layernorm): 1 + N(0, std) in bf16."""
+    g = _gen("cpu", seed, layer, 4, 13 + which)
+    return (1.0 + torch.randn(hidden, generator=g, dtype=torch.float32) * std).to(torch.bfloat16).to(device)
+
+
 class SyntheticLayer:
     """Lazily generated weights of one MoE layer (per-expert cache optional)."""
 

@@ -19,7 +19,7 @@ from collections import OrderedDict
 
 import torch
 
-from .synthetic import PROJS, SHARED, SyntheticLayer, expert_weights
+from .synthetic import PROJS, SHARED, SyntheticLayer, expert_weights, norm_weight
 
 
 class ExpertCache:
@@ -74,6 +74,7 @@ class SyntheticWeightStore:
         self._gate: dict[int, torch.Tensor] = {}
         self._bias: dict[int, torch.Tensor] = {}
         self._shared: dict[int, dict] = {}
+        self._norm: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
 
     def _seed(self, layer: int) -> int:
         return self.layer_seeds.get(layer, self.seed)
@@ -89,6 +90,15 @@ class SyntheticWeightStore:
         if layer not in self._gate:
             self._gate[layer] = self.layer(layer).gate.to(self.device)
         return self._gate[layer]
+
+    def get_layer_norm_weights(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """(input_layernorm, post_attention_layernorm) weights, as the
+        reference's ``WeightStore.get_layer_norm_weights`` (weight_store.py:228-234)."""
+        if layer not in self._norm:
+            c = self.config
+            self._norm[layer] = tuple(norm_weight(self._seed(layer), layer, i, c.hidden_size, self.device)
+                                      for i in (0, 1))
+        return self._norm[layer]
 
     def get_gate_bias(self, layer: int) -> torch.Tensor:
         if layer not in self._bias:

@@ -123,8 +123,10 @@ DSMOE_API size_t dsmoe_expert_ffn_workspace_size(int32_t tokens, int32_t hidden,
 DSMOE_API size_t dsmoe_fp8_linear_workspace_size(int32_t tokens, int32_t in_features, int32_t out_features);
 
 /*
- * One expert FFN. Replaces expert_ffn() / swiglu() (inference/ops.py:186-206):
- * down(silu(gate(x)) * up(x)).   x [tokens, hidden] bf16 -> out [tokens, hidden] bf16.
+ * One expert FFN. Replaces expert_ffn() / swiglu() / dense_ffn()
+ * (inference/ops.py:186-206): down(silu(gate(x)) * up(x)).
+ * x [tokens, hidden] bf16 -> out [tokens, hidden] bf16; hidden and inter are
+ * multiples of 128 up to 32768 (the dense layers 0-2 use inter = 18432).
  */
 DSMOE_API int dsmoe_expert_ffn(const void* x, int32_t tokens, int32_t hidden, int32_t inter, const void* w_gate,
                      const float* s_gate, const void* w_up, const float* s_up, const void* w_down,
@@ -133,7 +135,7 @@ DSMOE_API int dsmoe_expert_ffn(const void* x, int32_t tokens, int32_t hidden, in
 
 /*
  * FP8 block-quantised linear. Replaces fp8_linear() (inference/ops.py:15-44)
- * for in/out features that are multiples of 128:
+ * for in/out features that are multiples of 128, up to 32768:
  *   out[t, o] = bf16( sum_i x[t, i] * weight[o, i] * scale_inv[o/128, i/128] ).
  */
 DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_features, int32_t out_features,
@@ -149,6 +151,32 @@ DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_feature
  * [5] after the down GEMM, [6] after the combine. n = 0 switches it off.
  */
 DSMOE_API int dsmoe_set_profile_events(void* const* events, int32_t n);
+
+/*
+ * RMSNorm, replaces `rms_norm` (inference/ops.py:10-13):
+ *   out = bf16( bf16(x * 1/sqrt(mean(x^2) + eps)) * weight )
+ * x, out [tokens][hidden] bf16, weight [hidden] bf16, hidden % 8 == 0, all
+ * 16-byte aligned. The row mean is summed in a different order from torch's
+ * CPU reduction, so 1/sqrt may differ from the reference in its last bit.
+ */
+DSMOE_API int dsmoe_rms_norm(const void* x, const void* weight, float eps, int32_t tokens, int32_t hidden,
+                             void* out, dsmoe_stream_t stream);
+
+/*
+ * The FFN half of a MoE transformer layer, replaces
+ * inference/forward.py:97-109 for layers >= first_k_dense_replace:
+ *   out = hidden + moe_block(rms_norm(hidden, norm_weight, eps))
+ * (bf16 residual add fused into the combine). `norm_weight` is the layer's
+ * post_attention_layernorm weight [hidden] bf16; other arguments as for
+ * dsmoe_moe_forward; the workspace is dsmoe_moe_layer_ffn_workspace_size
+ * bytes (dsmoe_workspace_size plus the normalised activations). `out` must
+ * not alias `hidden`.
+ */
+DSMOE_API size_t dsmoe_moe_layer_ffn_workspace_size(const dsmoe_moe_config_t* cfg, int32_t tokens);
+DSMOE_API int dsmoe_moe_layer_ffn(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* weights,
+                                  const void* hidden, const void* norm_weight, float eps, int32_t tokens, void* out,
+                                  int64_t* topk_idx, float* topk_w, void* workspace, size_t workspace_bytes,
+                                  dsmoe_stream_t stream);
 
 /*
  * Overlap hook (no reference counterpart; the reference has no collectives).

@@ -8,10 +8,13 @@ extension is missing.
 It restates, in plain torch-on-CPU fp32/bf16 arithmetic, the reference
 algorithm of ``sushruta/deepseek-on-one-gpu``:
 
+  * ``rms_norm``       — ``inference/ops.py:10-13``
   * ``route_ref``      — ``inference/ops.py:209-257``
   * ``fp8_linear``     — ``inference/ops.py:15-44``
   * ``expert_ffn``     — ``inference/ops.py:186-192, 202-206``
   * ``moe_block_literal`` — ``inference/forward.py:112-153`` (per-token loop)
+  * ``moe_layer_ffn``  — ``inference/forward.py:97-109`` (the MoE layer's FFN
+    half: ``hidden + moe_block(rms_norm(hidden, post_attention_layernorm))``)
   * ``moe_block_grouped`` — the same arithmetic grouped by expert, for sizes the
     literal loop cannot finish in seconds. Per element it performs the same
     fp32 dequant, fp32 dot products, bf16 roundings and bf16 combine order;
@@ -91,6 +94,16 @@ def route_v3(hidden: torch.Tensor, gate_weight: torch.Tensor, bias: torch.Tensor
     w = s.gather(-1, idx)
     w = w / w.sum(dim=-1, keepdim=True)
     return idx, w * routed_scaling_factor
+
+
+# --------------------------------------------------------------------------
+# RMSNorm
+# --------------------------------------------------------------------------
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """``inference/ops.py:10-13``: fp32 mean of squares, rsqrt, the product
+    rounded to x's dtype, then the bf16 product with the weight."""
+    r = torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + eps)
+    return (x.float() * r).to(x.dtype) * weight
 
 
 # --------------------------------------------------------------------------
@@ -177,6 +190,15 @@ def moe_block_grouped(hidden: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, 
     scale = routed_scaling_factor if final_scale is None else final_scale
     out = shared_out + routed * scale
     return out.reshape(hidden.shape)
+
+
+def moe_layer_ffn(hidden: torch.Tensor, ln_weight: torch.Tensor, eps: float, gate_weight: torch.Tensor,
+                  get_expert, shared: dict, **kw) -> torch.Tensor:
+    """``inference/forward.py:97-109`` for a MoE layer: the block on the
+    RMS-normalised hidden state, plus the residual (a bf16 add)."""
+    normed = rms_norm(hidden, ln_weight, eps)
+    idx, w = route_ref(normed, gate_weight)
+    return hidden + moe_block_grouped(normed, idx, w, get_expert, shared, **kw)
 
 
 def rel_rms(a: torch.Tensor, b: torch.Tensor) -> float:

@@ -4,9 +4,12 @@ Run (needs the reference source tree; not needed to run the tests):
 
     python tests/golden/make_golden.py /path/to/deepseek-on-one-gpu
 
-It imports the reference's own ``inference.ops.route`` and
-``inference.forward.moe_block`` (``inference/ops.py:209-257``,
-``inference/forward.py:112-153``) unchanged and runs them on CPU. The three
+It imports the reference's own ``inference.ops.route``, ``inference.ops.rms_norm``
+and ``inference.forward.moe_block`` (``inference/ops.py:209-257``,
+``inference/ops.py:10-13``, ``inference/forward.py:112-153``) unchanged and runs
+them on CPU. The "layer_ffn" cases compose them exactly as the MoE layer's
+FFN half does (``inference/forward.py:97-109``): ``hidden +
+moe_block(rms_norm(hidden, post_attention_layernorm))``. The three
 objects ``moe_block`` touches (``weight_store.get_gate_weight``,
 ``weight_store.get_shared_expert_weights``, ``gpu_transfer.transfer_experts``,
 ``inference/forward.py:121,133,147``) are served by in-memory stubs that hand
@@ -28,7 +31,7 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO / "deepseek-on-one-gpu_b200"))
 
-from dsmoe.synthetic import SyntheticLayer, activations  # noqa: E402
+from dsmoe.synthetic import SyntheticLayer, activations, norm_weight  # noqa: E402
 
 # name: (seed, T, H, F, E, kind)
 CASES = {
@@ -37,7 +40,11 @@ CASES = {
     "tiny_t1": (102, 1, 512, 256, 256, "block"),
     "c1_t8_full": (0, 8, 7168, 2048, 256, "block"),
     "route_t512_full": (1, 512, 7168, 2048, 256, "route"),
+    "ffn_t16": (103, 16, 512, 256, 256, "layer_ffn"),
+    "ffn_c1_t8_full": (0, 8, 7168, 2048, 256, "layer_ffn"),
+    "norm_t16_full": (104, 16, 7168, 2048, 256, "norm"),
 }
+EPS = 1e-6
 LAYER = 3
 
 
@@ -78,6 +85,10 @@ def main(ref_root: str) -> None:
         cfg = RefConfig(hidden_size=H, moe_intermediate_size=F, n_routed_experts=E)
         layer = SyntheticLayer(seed, LAYER, H, F, E)
         x = activations(seed, T, H).view(1, T, H)
+        hidden = x
+        if kind in ("layer_ffn", "norm"):
+            ln = norm_weight(seed, LAYER, 1, H)
+            x = ref_ops.rms_norm(hidden, ln, EPS)  # the MoE block's input
         idx, w = ref_ops.route(x, layer.gate, cfg)
         rec = dict(seed=seed, T=T, H=H, F=F, E=E, layer=LAYER, kind=kind,
                    n_group=cfg.n_group, topk_group=cfg.topk_group,
@@ -85,8 +96,14 @@ def main(ref_root: str) -> None:
                    routed_scaling_factor=cfg.routed_scaling_factor,
                    idx=idx.reshape(T, -1).clone(), w=w.reshape(T, -1).clone(),
                    torch_version=str(torch.__version__))
-        if kind == "block":
+        if kind in ("layer_ffn", "norm"):
+            rec["eps"] = EPS
+            rec["normed"] = x.reshape(T, H).clone()
+        if kind in ("block", "layer_ffn"):
             out = ref_forward.moe_block(x, LAYER, StubWeightStore(layer), StubTransfer(layer), cfg)
+            if kind == "layer_ffn":
+                rec["moe"] = out.reshape(T, H).clone()  # the block's output before the residual add
+                out = hidden + out
             rec["out"] = out.reshape(T, H).clone()
         torch.save(rec, HERE / f"{name}.pt")
         print(f"{name}: {time.time() - t0:.1f}s", flush=True)

@@ -84,7 +84,9 @@ def test_forward_rejects_bad_weights():
 def test_ffn_and_linear_reject_unsupported_shapes():
     L = _lib.lib()
     assert L.dsmoe_expert_ffn(32, 8, 100, 256, 32, 32, 32, 32, 32, 32, 32, 32, 1 << 40, None) == -4
-    assert L.dsmoe_fp8_linear(32, 8, 7168, 576, 32, 32, 32, 32, 1 << 40, None) == -4
+    assert L.dsmoe_fp8_linear(32, 8, 7168, 100, 32, 32, 32, 32, 1 << 40, None) == -4  # out % 8
+    assert L.dsmoe_fp8_linear(32, 8, 7100, 512, 32, 32, 32, 32, 1 << 40, None) == -4  # in % 128
+    assert L.dsmoe_expert_ffn(32, 8, 7168, 40960, 32, 32, 32, 32, 32, 32, 32, 32, 1 << 40, None) == -4
     assert L.dsmoe_fp8_linear(32, 0, 7168, 512, 32, 32, 32, 32, 1 << 40, None) == 0
 
 

@@ -1,13 +1,13 @@
 """The CPU oracle is pinned to the reference: golden vectors in tests/golden
-are outputs of the reference's own route() and moe_block() (made by
-tests/golden/make_golden.py)."""
+are outputs of the reference's own route(), rms_norm() and moe_block() (made
+by tests/golden/make_golden.py)."""
 import os
 
 import pytest
 import torch
 
 from conftest import GOLDEN
-from dsmoe.synthetic import SyntheticLayer, activations
+from dsmoe.synthetic import SyntheticLayer, activations, norm_weight
 from oracle import moe_oracle as O
 
 BLOCK_CASES = ["small_t16", "mid_t33", "tiny_t1", "c1_t8_full"]
@@ -83,3 +83,29 @@ def test_index_parity_tie_rule():
     c = torch.tensor([[0, 3]])
     bad, ties = O.index_parity(a, c, scores)
     assert (bad, ties) == (1, 0)
+
+
+NORM_CASES = ["norm_t16_full", "ffn_t16", "ffn_c1_t8_full"]
+
+
+@pytest.mark.parametrize("name", NORM_CASES)
+def test_rms_norm_matches_reference_exactly(name):
+    g = load(name)
+    x = activations(g["seed"], g["T"], g["H"])
+    normed = O.rms_norm(x, norm_weight(g["seed"], g["layer"], 1, g["H"]), g["eps"])
+    assert torch.equal(normed, g["normed"])
+
+
+@pytest.mark.parametrize("name", ["ffn_t16", "ffn_c1_t8_full"])
+def test_layer_ffn_close(name):
+    """hidden + moe_block(rms_norm(hidden)): the routing on the normalised
+    input equals the reference's; the output matches up to the fp32 GEMM
+    summation order of the grouped restatement."""
+    g = load(name)
+    layer, x = inputs(g)
+    normed = O.rms_norm(x, norm_weight(g["seed"], g["layer"], 1, g["H"]), g["eps"])
+    idx, w = O.route_ref(normed, layer.gate)
+    assert torch.equal(idx, g["idx"]) and torch.equal(w, g["w"])
+    out = O.moe_layer_ffn(x, norm_weight(g["seed"], g["layer"], 1, g["H"]), g["eps"], layer.gate, layer.expert,
+                          layer.shared())
+    assert O.rel_rms(out, g["out"]) < 1e-3
