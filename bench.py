@@ -53,6 +53,49 @@ def gemm_tile(tokens: int) -> int:
     return 32 if tokens <= 32 else 64 if tokens <= 64 else 128 if tokens <= 128 else 160
 
 
+def expert_load_rates(cfg, dev, n_experts: int = 16, layer: int = 7) -> dict:
+    """Expert disk step (SURVEY's first widening row): read n R1-size experts
+    from a safetensors file (written just before, so from the page cache)
+    into pinned host memory, with the store (packed buffers, native pread
+    pool) and with the reference's own steps (safe_open, get_tensor, copy into
+    a fresh pinned tensor; oracle/expert_loader.py). Each is timed on its
+    second pass, after torch's pinned allocator has warmed up."""
+    import tempfile
+
+    from safetensors.torch import save_file
+
+    from dsmoe.safetensors_store import SafetensorsWeightStore
+    from dsmoe.synthetic import expert_weights
+    from oracle.expert_loader import load_expert, shard_map
+
+    tensors = {}
+    for e in range(n_experts):
+        for proj, (w, s) in expert_weights(21, layer, e, cfg.hidden_size, cfg.moe_intermediate_size, "cuda").items():
+            pre = f"model.layers.{layer}.mlp.experts.{e}.{proj}"
+            tensors[pre + ".weight"] = w.cpu()
+            tensors[pre + ".weight_scale_inv"] = s.cpu()
+    nbytes = sum(t.nbytes for t in tensors.values())
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        save_file(tensors, os.path.join(td, "model.safetensors"))
+        del tensors
+        for rep in range(2):
+            store = SafetensorsWeightStore(td, cfg, dev, expert_cache_bytes=1 << 40, threads=16)
+            t0 = time.perf_counter()
+            got = [store.get_expert(layer, e) for e in range(n_experts)]
+            t1 = time.perf_counter()
+            del got, store
+            k2s = shard_map(td)
+            t2 = time.perf_counter()
+            ref = [load_expert(td, k2s, layer, e) for e in range(n_experts)]
+            t3 = time.perf_counter()
+            del ref
+        out = {"expert_load_GB_s": nbytes / (t1 - t0) / 1e9, "reference_loader_GB_s": nbytes / (t3 - t2) / 1e9,
+               "expert_load_sample": f"{n_experts} R1 experts ({nbytes / 1e9:.2f} GB) from the page cache into "
+                                     f"pinned host memory, 16 pread threads"}
+    return out
+
+
 def peaks():
     """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     try:
@@ -565,10 +608,11 @@ def main():
         dense_w = {p: (w.to(dev), s.to(dev)) for p, (w, s) in expert_weights(5, 0, 0, H, 18432, "cuda").items()}
         dn_ms = dev_ms(lambda: dense_ffn(x, dense_w))
         dense_bytes = 3 * 18432 * H + T * H * 2 * 2
+        loader = expert_load_rates(cfg, dev)
         widened = {"rms_norm_ms": norm_ms, "rms_norm_GB_s": 2 * T * H * 2 / (norm_ms / 1e3) / 1e9,
                    "moe_layer_ffn_ms": ffn_ms, "moe_layer_ffn_over_block": ffn_ms / ms_max,
                    "dense_ffn_ms": dn_ms, "dense_ffn_tflops": 2.0 * T * 3 * 18432 * H / (dn_ms / 1e3) / 1e12,
-                   "dense_ffn_weight_GB": dense_bytes / 1e9}
+                   "dense_ffn_weight_GB": dense_bytes / 1e9, **loader}
         del dense_w
     status = Workspace.get(dev).status()
 

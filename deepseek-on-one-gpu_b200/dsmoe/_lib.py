@@ -24,7 +24,7 @@ EXPORTED = (
     "dsmoe_expert_ffn", "dsmoe_fp8_linear", "dsmoe_read_status", "dsmoe_set_profile_events",
     "dsmoe_expert_ffn_noalloc", "dsmoe_ep_dispatch", "dsmoe_moe_local_workspace_size", "dsmoe_moe_local",
     "dsmoe_ep_combine", "dsmoe_set_gemm_sm_limit", "dsmoe_rms_norm", "dsmoe_moe_layer_ffn_workspace_size",
-    "dsmoe_moe_layer_ffn",
+    "dsmoe_moe_layer_ffn", "dsmoe_read_ranges",
 )
 
 
@@ -88,6 +88,9 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_moe_layer_ffn_workspace_size.argtypes = [cfgp, i32]
                 L.dsmoe_moe_layer_ffn_workspace_size.restype = sz
                 L.dsmoe_moe_layer_ffn.argtypes = [cfgp, wp, vp, vp, ctypes.c_float, i32, vp, vp, vp, vp, sz, vp]
+                u64p = ctypes.POINTER(ctypes.c_uint64)
+                L.dsmoe_read_ranges.argtypes = [i32, ctypes.POINTER(ctypes.c_char_p), u64p, u64p,
+                                                ctypes.POINTER(vp), i32]
                 for name in EXPORTED:
                     getattr(L, name).restype = getattr(L, name).restype or ctypes.c_int
                 _lib = L

@@ -32,7 +32,7 @@ class ExpertCache:
 
     @staticmethod
     def entry_bytes(expert_dict: dict) -> int:
-        return sum(t.nbytes for proj in expert_dict.values() for t in proj.values())
+        return sum(t.nbytes for proj in expert_dict.values() if isinstance(proj, dict) for t in proj.values())
 
     def get(self, layer: int, expert_idx: int) -> dict | None:
         key = (layer, expert_idx)

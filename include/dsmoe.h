@@ -179,6 +179,18 @@ DSMOE_API int dsmoe_moe_layer_ffn(const dsmoe_moe_config_t* cfg, const dsmoe_lay
                                   dsmoe_stream_t stream);
 
 /*
+ * Host-side expert loader, replaces the disk read of
+ * WeightStore._load_expert_from_disk (inference/weight_store.py:151-180):
+ * copies n byte ranges (paths[i], offsets[i], sizes[i]) of safetensors shard
+ * files into host buffers dsts[i] (pinned, typically one packed buffer per
+ * expert) with pread on `threads` threads (1..64), ranges cut into 8 MiB
+ * pieces. No GPU work. Returns DSMOE_ERR_INVALID for a missing file or a
+ * range past its end.
+ */
+DSMOE_API int dsmoe_read_ranges(int32_t n, const char* const* paths, const uint64_t* offsets, const uint64_t* sizes,
+                                void* const* dsts, int32_t threads);
+
+/*
  * Overlap hook (no reference counterpart; the reference has no collectives).
  * Caps the persistent grid of the calling thread's later grouped-GEMM
  * launches at max_ctas CTAs (one per SM), leaving the other SMs free for a

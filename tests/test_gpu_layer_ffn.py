@@ -150,3 +150,43 @@ def test_fp8_linear_projection_shapes(T, I, O_):
     assert got.shape == (T, O_)
     ref = O.fp8_linear(x, wq, sc)
     assert O.rel_rms(got.float(), ref.float()) < REL_RMS_TOL
+
+
+def test_moe_block_streams_experts_from_safetensors(tmp_path):
+    """A checkpoint written in the R1 key layout, read by
+    SafetensorsWeightStore (packed pinned buffers, native range reads), streamed
+    into a 200-slot bank by GPUTransfer and run through moe_block, matches the
+    oracle on the same tensors."""
+    from safetensors.torch import save_file
+
+    from dsmoe.safetensors_store import SafetensorsWeightStore
+
+    H, F, E, layer = 512, 256, 256, 5
+    cfg = DeepSeekConfig(hidden_size=H, moe_intermediate_size=F)
+    tensors = {}
+    for e in list(range(E)) + ["shared"]:
+        w = expert_weights(11, layer, 300 if e == "shared" else e, H, F)
+        pre = f"model.layers.{layer}.mlp." + ("shared_experts." if e == "shared" else f"experts.{e}.")
+        for proj, (q, s) in w.items():
+            tensors[pre + proj + ".weight"] = q
+            tensors[pre + proj + ".weight_scale_inv"] = s
+    gate = (torch.randn(E, H, generator=torch.Generator().manual_seed(12)) * 0.006).to(torch.bfloat16)
+    tensors[f"model.layers.{layer}.mlp.gate.weight"] = gate
+    save_file(tensors, str(tmp_path / "model.safetensors"))
+    store = SafetensorsWeightStore(tmp_path, cfg, DEV, expert_cache_bytes=1 << 30)
+    gt = GPUTransfer(cfg, store, DEV, slots_per_layer=200)  # 24 tokens use at most 192 experts
+    x = activations(13, 24, H)
+    out = moe_block(x.to(DEV), layer, store, gt, cfg).cpu()
+    assert gt.slot_misses > 0 and store.bytes_read > 0
+    idx, w = O.route_ref(x, gate)
+
+    def expert(e):
+        pre = f"model.layers.{layer}.mlp.experts.{e}."
+        return {p: (tensors[pre + p + ".weight"], tensors[pre + p + ".weight_scale_inv"])
+                for p in ("gate_proj", "up_proj", "down_proj")}
+
+    shared = {p: (tensors[f"model.layers.{layer}.mlp.shared_experts.{p}.weight"],
+                  tensors[f"model.layers.{layer}.mlp.shared_experts.{p}.weight_scale_inv"])
+              for p in ("gate_proj", "up_proj", "down_proj")}
+    ref = O.moe_block_grouped(x, idx, w, expert, shared)
+    assert O.rel_rms(out.float(), ref.float()) < REL_RMS_TOL
