@@ -79,9 +79,10 @@ struct Cfg {
   static constexpr int NUM_BARS = 2 * STAGES + 2 * NBUF + 1;
   static constexpr int MISC_OFF = BAR_OFF + 8 * NUM_BARS;
   static constexpr int TABLE_OFF = ((MISC_OFF + 16 + 15) / 16) * 16;
-  // the per-group tables stay in global memory (L1-cached): shared memory
-  // goes to the stage ring
-  static constexpr int SMEM_BYTES = TABLE_OFF + 1024;  // + alignment slack
+  // Of the per-group tables only the unit prefix sums (searched at every
+  // unit start) live in shared memory; the rest is read from global memory
+  // (L1-cached), so that shared memory goes to the stage ring.
+  static constexpr int SMEM_BYTES = TABLE_OFF + 4 * MAX_GROUPS + 1024;  // + alignment slack
   static_assert(BN % 32 == 0 && BN <= 256 && EPI_COLS % CHUNK == 0 && NBUF * TCOLS <= 512 &&
                     (!NCAT || 2 * BN <= 256), "tile shape");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
@@ -124,7 +125,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   uint64_t* done_bar = tempty + NBUF;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
-  const int* __restrict__ s_ustart = p.unit_start;
+  int* s_ustart = reinterpret_cast<int*>(smem + C::TABLE_OFF);
   const int* __restrict__ s_counts = p.counts;
   const int* __restrict__ s_rows = p.row_start;
   const int* __restrict__ s_slot = p.slot_of;
@@ -133,6 +134,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   const int lane = threadIdx.x & 31;
   const int NG = p.n_groups;
 
+  for (int i = threadIdx.x; i <= NG; i += blockDim.x) s_ustart[i] = p.unit_start[i];
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -343,14 +345,27 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         if (++tb == NBUF) { tb = 0; tphase ^= 1; }
       }
       if (!ok) break;
-      const int row_in_mat = (mt - mat * mt_per_mat) * BM + quad * 32 + lane;
-      const int feat = mat * p.M + row_in_mat;
-      const bool row_ok = row_in_mat < p.M;
+      // Stores of bf16 pairs: for tokens i and i+1, an even lane writes
+      // features (lane, lane+1) of token i and its odd neighbour features
+      // (lane-1, lane) of token i+1; one shuffle exchanges the halves.
+      const int odd = lane & 1;
+      const int row_in_mat = (mt - mat * mt_per_mat) * BM + quad * 32 + (lane & ~1);  // the pair's first row
+      const bool row_ok = row_in_mat < p.M;  // M is even: the pair is inside or outside together
+      __nv_bfloat16* ybase = p.y + mat * p.M + row_in_mat;
 #pragma unroll
-      for (int i = 0; i < EPI_COLS; ++i) {
-        const float s = __shfl_sync(0xffffffffu, i < 32 ? sxa : sxb, i & 31);
-        if (i < nvalid && row_ok)
-          p.y[static_cast<size_t>(row_base + i) * out_ld + feat] = __float2bfloat16_rn(acc[i] * s);
+      for (int i = 0; i < EPI_COLS; i += 2) {
+        const float s0 = __shfl_sync(0xffffffffu, i < 32 ? sxa : sxb, i & 31);
+        const float s1 = __shfl_sync(0xffffffffu, i + 1 < 32 ? sxa : sxb, (i + 1) & 31);
+        const __nv_bfloat16 v0 = __float2bfloat16_rn(acc[i] * s0);
+        const __nv_bfloat16 v1 = __float2bfloat16_rn(acc[i + 1] * s1);
+        const unsigned short mine = __bfloat16_as_ushort(odd ? v1 : v0);
+        const unsigned short other = static_cast<unsigned short>(
+            __shfl_xor_sync(0xffffffffu, static_cast<unsigned int>(__bfloat16_as_ushort(odd ? v0 : v1)), 1));
+        const uint32_t pair = odd ? (static_cast<uint32_t>(other) | (static_cast<uint32_t>(mine) << 16))
+                                  : (static_cast<uint32_t>(mine) | (static_cast<uint32_t>(other) << 16));
+        const int tok = i + odd;
+        if (tok < nvalid && row_ok)
+          *reinterpret_cast<uint32_t*>(ybase + static_cast<size_t>(row_base + tok) * out_ld) = pair;
       }
     }
   }
