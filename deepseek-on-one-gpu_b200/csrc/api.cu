@@ -307,8 +307,9 @@ int run_ffn(const void* w_gate, const float* s_gate, const void* w_up, const flo
   j.y = at<__nv_bfloat16>(ws, L.gu);
   if ((r = run_gemm(j, s))) return r;
   prof(3, s);
-  DSMOE_CUDA(launch_swiglu_quant(at<__nv_bfloat16>(ws, L.gu), F, at<int32_t>(ws, L.row_start) + n_groups, L.P,
-                                 at<uint8_t>(ws, L.hq), at<float>(ws, L.hs), s));
+  DSMOE_CUDA(launch_swiglu_quant(at<__nv_bfloat16>(ws, L.gu), F, at<int32_t>(ws, L.row_start),
+                                 at<int32_t>(ws, L.counts), n_groups, L.P, at<uint8_t>(ws, L.hq), at<float>(ws, L.hs),
+                                 s));
   prof(4, s);
   j.w0 = j.w1 = w_down;
   j.s0 = j.s1 = s_down;

@@ -39,8 +39,9 @@ cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, co
                                 const CUtensorMap& x32, const GemmParams& p, int tile, int grid, cudaStream_t stream);
 
 // SwiGLU + hi/lo split (swiglu_quant.cu)
-cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_end, int P, uint8_t* hq,
-                                float* hs, cudaStream_t stream);
+// rows of real (token, group) pairs only: row_start[n_groups + 1], counts[n_groups]
+cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_start, const int32_t* counts,
+                                int n_groups, int P, uint8_t* hq, float* hs, cudaStream_t stream);
 
 // Router (router_tc.cu logits, router.cu selection)
 int router_tc_ksplit(int T, int H, int num_sms);

@@ -6,7 +6,7 @@
 //   count   histogram of (token, k) pairs per expert group
 //   plan    exclusive scans -> 32-row-aligned segment starts, work-unit starts
 //           of both GEMMs (one block)
-//   scatter one warp per token: claims one row in each of its experts'
+//   scatter one CTA per token: claims one row in each of its experts'
 //           segments (+ its row in the shared-expert segment), splits the bf16
 //           row into hi/lo e4m3 terms with one fp32 scale per row, writes the
 //           row copies and records the (token, k) -> row map used by the
@@ -79,79 +79,118 @@ __global__ void __launch_bounds__(MAX_GROUPS) plan_kernel(int32_t* __restrict__ 
   if (i < n_groups) cursor[i] = 0;
 }
 
-__global__ void __launch_bounds__(256) quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
-                                                            const int32_t* __restrict__ idx, int top_k, int n_groups,
-                                                            int has_shared, const int32_t* __restrict__ row_start,
-                                                            int32_t* __restrict__ cursor, int P,
-                                                            uint8_t* __restrict__ xq, float* __restrict__ sx,
-                                                            int32_t* __restrict__ pos) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  int myrow = -1;
-  if (lane < top_k) {
-    const int g = idx[static_cast<size_t>(t) * top_k + lane] + 1;  // entries < 0 (no expert) are skipped
+// hi/lo split of 8 values (already multiplied by 448 / amax), packed.
+__device__ __forceinline__ void split8(const uint4 v, float inv, uint2& hv, uint2& lv) {
+  const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
+  uint32_t hw[2], lw[2];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const float q0 = __bfloat162float(vb[i]) * inv, q1 = __bfloat162float(vb[i + 1]) * inv;
+    const uint16_t h2 = f32x2_to_e4m3x2(q0, q1);
+    const uint16_t l2 = f32x2_to_e4m3x2(q0 - e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff)),
+                                        q1 - e4m3_to_f32(static_cast<uint8_t>(h2 >> 8)));
+    if ((i & 2) == 0) {
+      hw[i >> 2] = h2;
+      lw[i >> 2] = l2;
+    } else {
+      hw[i >> 2] |= static_cast<uint32_t>(h2) << 16;
+      lw[i >> 2] |= static_cast<uint32_t>(l2) << 16;
+    }
+  }
+  hv = make_uint2(hw[0], hw[1]);
+  lv = make_uint2(lw[0], lw[1]);
+}
+
+__device__ __forceinline__ float amax8(const uint4 v, float m) {
+  const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(__bfloat162float(vb[i])));
+  return m;
+}
+
+// One CTA of QS_THREADS per token: the token's rows are placed (one atomic
+// per routed expert), its row amax is reduced over the CTA, and its hi/lo
+// split is written to every row it occupies (the shared-expert row and one
+// per routed expert). Rows of up to QS_THREADS * 8 * QS_MAXC columns stay in
+// registers between the two passes; wider rows are read twice.
+constexpr int QS_THREADS = 256;
+constexpr int QS_MAXC = 4;
+
+__global__ void __launch_bounds__(QS_THREADS) quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                                   const int32_t* __restrict__ idx, int top_k,
+                                                                   int n_groups, int has_shared,
+                                                                   const int32_t* __restrict__ row_start,
+                                                                   int32_t* __restrict__ cursor, int P,
+                                                                   uint8_t* __restrict__ xq, float* __restrict__ sx,
+                                                                   int32_t* __restrict__ pos) {
+  const int t = blockIdx.x;
+  __shared__ int s_rows[9];
+  __shared__ float s_red[QS_THREADS / 32];
+  const int tid = threadIdx.x;
+  if (tid < top_k) {
+    const int g = idx[static_cast<size_t>(t) * top_k + tid] + 1;  // entries < 0 (no expert) are skipped
+    int myrow = -1;
     if (g >= 1 && g < n_groups) myrow = row_start[g] + atomicAdd(&cursor[g], 1);
-    pos[static_cast<size_t>(t) * top_k + lane] = myrow;
+    pos[static_cast<size_t>(t) * top_k + tid] = myrow;
+    s_rows[has_shared + tid] = myrow;
   }
-  int rows[9];
-  int n = 0;
-  if (has_shared) rows[n++] = row_start[0] + t;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int r = __shfl_sync(0xffffffffu, myrow, k);
-    if (k < top_k) rows[has_shared + k] = r;
-  }
-  n += top_k;
+  if (tid == 0 && has_shared) s_rows[0] = row_start[0] + t;
+  const int n = has_shared + top_k;
   const __nv_bfloat16* xr = x + static_cast<size_t>(t) * H;
-  uint8_t* xq_lo = xq + static_cast<size_t>(P) * H;
-  // pass 1: row amax (each lane covers 8 consecutive columns per 256)
+  const uint4* xv = reinterpret_cast<const uint4*>(xr);
+  const int nchunks = H / 8;
+  const bool in_regs = nchunks <= QS_THREADS * QS_MAXC;
+  uint4 v[QS_MAXC];
   float amax = 0.f;
-  for (int col = lane * 8; col < H; col += 256) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + col));
-    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
+  if (in_regs) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(vb[i])));
+    for (int i = 0; i < QS_MAXC; ++i) {
+      const int c = tid + i * QS_THREADS;
+      if (c < nchunks) {
+        v[i] = __ldg(xv + c);
+        amax = amax8(v[i], amax);
+      }
+    }
+  } else {
+    for (int c = tid; c < nchunks; c += QS_THREADS) amax = amax8(__ldg(xv + c), amax);
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float inv = amax > 0.f ? 448.f / amax : 0.f;
-  if (lane < n) {
-    int rr = rows[0];
+  if ((tid & 31) == 0) s_red[tid >> 5] = amax;
+  __syncthreads();  // also publishes s_rows
+  amax = s_red[0];
 #pragma unroll
-    for (int r = 1; r < 9; ++r)
-      if (r == lane) rr = rows[r];
+  for (int i = 1; i < QS_THREADS / 32; ++i) amax = fmaxf(amax, s_red[i]);
+  const float inv = amax > 0.f ? 448.f / amax : 0.f;
+  int rows[9];
+#pragma unroll
+  for (int r = 0; r < 9; ++r) rows[r] = r < n ? s_rows[r] : -1;
+  if (tid < n) {
+    const int rr = s_rows[tid];
     if (rr >= 0) sx[rr] = amax / 448.f;
   }
-  // pass 2: split and write every copy of the row
-  for (int col = lane * 8; col < H; col += 256) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + col));
-    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v);
-    uint32_t hw[2], lw[2];
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      const float q0 = __bfloat162float(vb[i]) * inv, q1 = __bfloat162float(vb[i + 1]) * inv;
-      const uint16_t h2 = f32x2_to_e4m3x2(q0, q1);
-      const uint16_t l2 = f32x2_to_e4m3x2(q0 - e4m3_to_f32(static_cast<uint8_t>(h2 & 0xff)),
-                                          q1 - e4m3_to_f32(static_cast<uint8_t>(h2 >> 8)));
-      if ((i & 2) == 0) {
-        hw[i >> 2] = h2;
-        lw[i >> 2] = l2;
-      } else {
-        hw[i >> 2] |= static_cast<uint32_t>(h2) << 16;
-        lw[i >> 2] |= static_cast<uint32_t>(l2) << 16;
-      }
-    }
-    const uint2 hv = make_uint2(hw[0], hw[1]);
-    const uint2 lv = make_uint2(lw[0], lw[1]);
+  uint8_t* xq_lo = xq + static_cast<size_t>(P) * H;
+  auto write = [&](int c, const uint4& val) {
+    uint2 hv, lv;
+    split8(val, inv, hv, lv);
+    const int col = c * 8;
 #pragma unroll
     for (int r = 0; r < 9; ++r) {
-      if (r < n && rows[r] >= 0) {
+      if (rows[r] >= 0) {
         const size_t off = static_cast<size_t>(rows[r]) * H + col;
         *reinterpret_cast<uint2*>(xq + off) = hv;
         *reinterpret_cast<uint2*>(xq_lo + off) = lv;
       }
     }
+  };
+  if (in_regs) {
+#pragma unroll
+    for (int i = 0; i < QS_MAXC; ++i) {
+      const int c = tid + i * QS_THREADS;
+      if (c < nchunks) write(c, v[i]);
+    }
+  } else {
+    for (int c = tid; c < nchunks; c += QS_THREADS) write(c, __ldg(xv + c));
   }
 }
 }  // namespace pm
@@ -180,9 +219,10 @@ cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx
                                  int has_shared, const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq,
                                  float* sx, int32_t* pos, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  const int blocks = (T * 32 + 255) / 256;
-  pm::quant_scatter_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, idx, top_k,
-                                                       n_groups, has_shared, row_start, cursor, P, xq, sx, pos);
+  if (top_k + has_shared > 9) return cudaErrorInvalidValue;
+  pm::quant_scatter_kernel<<<T, pm::QS_THREADS, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, idx,
+                                                              top_k, n_groups, has_shared, row_start, cursor, P, xq,
+                                                              sx, pos);
   return cudaGetLastError();
 }
 

@@ -37,16 +37,26 @@ __global__ void __launch_bounds__(256) select_kernel(const float* __restrict__ p
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
   const float NEG = -CUDART_INF_F;
-  float s[8], key[8];
+  float s[8], key[8], lg[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) lg[g] = 0.f;
+  // The K-split partials are added in split order (fixed, deterministic); the
+  // eight groups' loads of one split are independent, so they are issued
+  // together.
+#pragma unroll 4
+  for (int k = 0; k < ksplit; ++k) {
+    const float* pk = partial + (static_cast<size_t>(k) * T + t) * E + lane;
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      if (g < n_group) lg[g] += __ldg(pk + g * 32);
+  }
 #pragma unroll
   for (int g = 0; g < 8; ++g) {
     s[g] = NEG;
     key[g] = NEG;
     if (g < n_group) {
       const int e = g * 32 + lane;
-      float l = 0.f;
-      for (int k = 0; k < ksplit; ++k) l += __ldg(partial + (static_cast<size_t>(k) * T + t) * E + e);
-      s[g] = 1.0f / (1.0f + expf(-l));
+      s[g] = 1.0f / (1.0f + expf(-lg[g]));
       key[g] = mode == 1 ? s[g] + __ldg(bias + e) : s[g];
     }
   }

@@ -51,14 +51,42 @@ __device__ __forceinline__ void split_store8(const float* q, uint8_t* hi_dst, ui
   *reinterpret_cast<uint2*>(lo_dst) = make_uint2(lw[0], lw[1]);
 }
 
+constexpr int MAX_GROUPS = 264;
+
+// Group tables of the permuted rows in shared memory: row r is a real
+// (token, expert) row if it lies in group g's segment below its count; the
+// 32-row padding at each segment's end is skipped (the down GEMM reads it but
+// discards the columns).
+__device__ __forceinline__ void load_tables(const int32_t* row_start, const int32_t* counts, int n_groups,
+                                            int* s_rs, int* s_cnt) {
+  for (int i = threadIdx.x; i <= n_groups; i += blockDim.x) {
+    s_rs[i] = row_start[i];
+    if (i < n_groups) s_cnt[i] = counts[i];
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ bool real_row(int row, int n_groups, const int* s_rs, const int* s_cnt) {
+  if (row >= s_rs[n_groups]) return false;
+  int lo = 0, hi = n_groups;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (s_rs[mid] <= row) lo = mid; else hi = mid;
+  }
+  return row - s_rs[lo] < s_cnt[lo];
+}
+
 // One pass, F <= 256 * NIT.
 template <int NIT>
 __global__ void __launch_bounds__(256) swiglu_quant_1pass(const __nv_bfloat16* __restrict__ gu, int F,
-                                                          const int32_t* __restrict__ row_end, int P,
+                                                          const int32_t* __restrict__ row_start,
+                                                          const int32_t* __restrict__ counts, int n_groups, int P,
                                                           uint8_t* __restrict__ hq, float* __restrict__ hs) {
+  __shared__ int s_rs[MAX_GROUPS + 1], s_cnt[MAX_GROUPS];
+  load_tables(row_start, counts, n_groups, s_rs, s_cnt);
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= *row_end) return;
+  if (!real_row(row, n_groups, s_rs, s_cnt)) return;
   const __nv_bfloat16* g_row = gu + static_cast<size_t>(row) * 2 * F;
   const __nv_bfloat16* u_row = g_row + F;
   uint4 gv[NIT], uv[NIT];
@@ -111,11 +139,14 @@ __global__ void __launch_bounds__(256) swiglu_quant_1pass(const __nv_bfloat16* _
 }
 
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* __restrict__ gu, int F,
-                                                           const int32_t* __restrict__ row_end, int P,
+                                                           const int32_t* __restrict__ row_start,
+                                                           const int32_t* __restrict__ counts, int n_groups, int P,
                                                            uint8_t* __restrict__ hq, float* __restrict__ hs) {
+  __shared__ int s_rs[MAX_GROUPS + 1], s_cnt[MAX_GROUPS];
+  load_tables(row_start, counts, n_groups, s_rs, s_cnt);
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= *row_end) return;
+  if (!real_row(row, n_groups, s_rs, s_cnt)) return;
   const __nv_bfloat16* g_row = gu + static_cast<size_t>(row) * 2 * F;
   const __nv_bfloat16* u_row = g_row + F;
   uint8_t* hi_row = hq + static_cast<size_t>(row) * F;
@@ -141,14 +172,15 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* 
 }
 }  // namespace sq
 
-cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_end, int P, uint8_t* hq,
-                                float* hs, cudaStream_t stream) {
+cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_start, const int32_t* counts,
+                                int n_groups, int P, uint8_t* hq, float* hs, cudaStream_t stream) {
   if (P == 0) return cudaSuccess;
+  if (n_groups < 1 || n_groups > sq::MAX_GROUPS) return cudaErrorInvalidValue;
   const int blocks = (P * 32 + 255) / 256;
   if (F <= 2048)
-    sq::swiglu_quant_1pass<8><<<blocks, 256, 0, stream>>>(gu, F, row_end, P, hq, hs);
+    sq::swiglu_quant_1pass<8><<<blocks, 256, 0, stream>>>(gu, F, row_start, counts, n_groups, P, hq, hs);
   else
-    sq::swiglu_quant_kernel<<<blocks, 256, 0, stream>>>(gu, F, row_end, P, hq, hs);
+    sq::swiglu_quant_kernel<<<blocks, 256, 0, stream>>>(gu, F, row_start, counts, n_groups, P, hq, hs);
   return cudaGetLastError();
 }
 
