@@ -669,7 +669,9 @@ def main():
                       "fp8_frac_of_nominal_dense": algo_flops / (ms_max / 1e3) / 1e12 / FP8_DENSE_NOMINAL_TFLOPS,
                       "experts_touched": touched},
             **({"widened_rows": widened} if widened else {}),
-            "gpu_launches": 9 * args.steps,
+            # library kernels per step: router 2, count/plan/scatter 3, GEMMs 2, swiglu 1, combine 1;
+            # expert-parallel: + dispatch 3, + shared-expert FFN 5 (its own plan/scatter/GEMMs/swiglu)
+            "gpu_launches": (18 if ep else 9) * args.steps,
             "device_status": status,
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -96,3 +96,22 @@ def test_no_cpu_fallback():
     cfg_ = DeepSeekConfig(hidden_size=256, moe_intermediate_size=256)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.route(torch.zeros(1, 4, 256, dtype=torch.bfloat16), torch.zeros(256, 256, dtype=torch.bfloat16), cfg_)
+
+
+def test_norm_and_layer_ffn_reject_bad_arguments():
+    """Argument checks of the RMSNorm and layer-FFN entry points (no GPU
+    work is reached)."""
+    from dsmoe import DeepSeekConfig
+    L = _lib.lib()
+    assert L.dsmoe_rms_norm(32, 32, ctypes.c_float(1e-6), 4, 100, 32, None) == -1  # hidden % 8
+    assert L.dsmoe_rms_norm(32, 32, ctypes.c_float(-1.0), 4, 512, 32, None) == -1  # eps < 0
+    assert L.dsmoe_rms_norm(None, 32, ctypes.c_float(1e-6), 4, 512, 32, None) == -1
+    assert L.dsmoe_rms_norm(32, 32, ctypes.c_float(1e-6), 0, 512, 32, None) == 0  # nothing to do
+    cfg = _lib.moe_config(DeepSeekConfig(hidden_size=512, moe_intermediate_size=256))
+    w = _lib.LayerWeights(gate_weight=32, score_bias=None, n_slots=257, w_gate=32, s_gate=32, w_up=32, s_up=32,
+                          w_down=32, s_down=32, slot_of_expert=32)
+    need = L.dsmoe_moe_layer_ffn_workspace_size(cfg, 16)
+    assert need > L.dsmoe_workspace_size(cfg, 16)
+    assert L.dsmoe_moe_layer_ffn(cfg, w, 64, 32, ctypes.c_float(1e-6), 16, 64, None, None, 32, need, None) == -1  # aliasing
+    assert L.dsmoe_moe_layer_ffn(cfg, w, 64, 32, ctypes.c_float(1e-6), 16, 96, None, None, 32, need - 1, None) == -3
+    assert L.dsmoe_moe_layer_ffn(cfg, w, 64, None, ctypes.c_float(1e-6), 16, 96, None, None, 32, need, None) == -1
