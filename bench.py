@@ -315,6 +315,8 @@ def main():
                     help="expert-parallel step: token chunks whose all-to-alls overlap the expert GEMMs (1 = none)")
     ap.add_argument("--sm-reserve", type=int, default=0,
                     help="expert-parallel step: SMs the grouped GEMMs leave to the all-to-alls while they overlap")
+    ap.add_argument("--peer", action="store_true",
+                    help="expert-parallel step: exchange rows through mapped peer buffers (no NCCL all-to-all)")
     ap.add_argument("--no-overlap", action="store_true",
                     help="expert-parallel step: exchange and GEMMs in one stream, one after the other")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
@@ -371,6 +373,8 @@ def main():
                            expert_source=store.device_expert)
         ep_layer.sm_reserve = args.sm_reserve
         ep_layer.overlap = not args.no_overlap
+        if args.peer:
+            ep_layer.use_peer_memory(cap=T)
         bank = None
         x = activations(1000 * seed + rank, T, H, device=dev)
 
@@ -654,8 +658,9 @@ def main():
                        "hottest_expert_over_mean": hottest_over_mean,
                        "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
                        "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU",
-                       **({"ep_overlap": not args.no_overlap, "ep_chunks": args.chunks, "ep_sm_reserve": args.sm_reserve}
-                          if ep else {})},
+                       **({"ep_exchange": "peer memory (IPC-mapped buffers)" if args.peer else "NCCL all-to-all",
+                            "ep_overlap": not args.no_overlap, "ep_chunks": args.chunks,
+                            "ep_sm_reserve": args.sm_reserve} if ep else {})},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2,
                     "copies": "pinned host buffers; H2D and D2H on their own streams, double-buffered, "
@@ -678,6 +683,8 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if ep:
+            ep_layer.close()  # peer buffers (a collective when in use)
         dist.barrier()
         dist.destroy_process_group()
 

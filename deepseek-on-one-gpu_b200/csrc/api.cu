@@ -589,15 +589,17 @@ size_t dsmoe_moe_local_workspace_size(const dsmoe_moe_config_t* cfg, int32_t row
   return plan_moe(rows, cfg->hidden, cfg->inter, cfg->n_routed, cfg->top_k).total;
 }
 
-int dsmoe_moe_local(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden, int32_t rows,
-                    const int32_t* local_idx, const float* local_w, void* partial_out, void* workspace,
-                    size_t workspace_bytes, dsmoe_stream_t stream) {
+static int moe_local_impl(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden,
+                          int32_t rows, const int32_t* local_idx, const float* local_w, void* partial_out,
+                          const int32_t* origin, const uint64_t* peer_out, int me, int cap, void* workspace,
+                          size_t workspace_bytes, dsmoe_stream_t stream) {
   int r = check_cfg(cfg);
   if (r) return r;
   if ((r = check_weights(cfg, w))) return r;
   if (rows < 0) return fail(DSMOE_ERR_INVALID, "rows < 0");
   if (rows == 0) return DSMOE_OK;
-  if (!hidden || !partial_out || !local_idx || !local_w || !aligned16(hidden) || !aligned16(partial_out))
+  if (!hidden || (!partial_out && !peer_out) || !local_idx || !local_w || !aligned16(hidden) ||
+      (partial_out && !aligned16(partial_out)) || (peer_out && !origin))
     return fail(DSMOE_ERR_INVALID, "moe_local: NULL or unaligned pointer");
   const Ws L = plan_moe(rows, cfg->hidden, cfg->inter, cfg->n_routed, cfg->top_k);
   if (!workspace || workspace_bytes < L.total)
@@ -619,8 +621,110 @@ int dsmoe_moe_local(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* 
                    w->slot_of_expert, NG, y, s)))
     return r;
   DSMOE_CUDA(launch_combine(y, rows, H, pos, local_w, K, row_start, 1.0f, 0, nullptr,
-                            static_cast<__nv_bfloat16*>(partial_out), s));
+                            static_cast<__nv_bfloat16*>(partial_out), s, origin, peer_out, me, cap));
   prof(6, s);
+  return DSMOE_OK;
+}
+
+int dsmoe_moe_local(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden, int32_t rows,
+                    const int32_t* local_idx, const float* local_w, void* partial_out, void* workspace,
+                    size_t workspace_bytes, dsmoe_stream_t stream) {
+  return moe_local_impl(cfg, w, hidden, rows, local_idx, local_w, partial_out, nullptr, nullptr, 0, 0, workspace,
+                        workspace_bytes, stream);
+}
+
+int dsmoe_ep_plan(const int64_t* topk_idx, const float* topk_w, int32_t tokens, int32_t top_k, int32_t world,
+                  int32_t experts_per_rank, int32_t* send_counts, int32_t* tok_rows, int32_t* send_tok,
+                  int32_t* send_idx, float* send_w, dsmoe_stream_t stream) {
+  if (tokens < 0 || top_k < 1 || top_k > 8 || world < 1 || world > 64 || experts_per_rank < 1)
+    return fail(DSMOE_ERR_INVALID, "ep_plan: bad sizes (tokens %d, top_k %d, world %d, experts/rank %d)", tokens,
+                top_k, world, experts_per_rank);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (tokens == 0) {
+    DSMOE_CUDA(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world, s));
+    return DSMOE_OK;
+  }
+  const void* ps[7] = {topk_idx, topk_w, send_counts, tok_rows, send_tok, send_idx, send_w};
+  for (const void* p : ps)
+    if (!p) return fail(DSMOE_ERR_INVALID, "ep_plan: NULL pointer");
+  DSMOE_CUDA(launch_ep_plan(topk_idx, topk_w, tokens, top_k, world, experts_per_rank, send_counts, tok_rows, send_tok,
+                            send_idx, send_w, s));
+  return DSMOE_OK;
+}
+
+int dsmoe_ep_push(const void* hidden, int32_t tokens, int32_t top_k, int32_t hidden_size, int32_t world, int32_t rank,
+                  int32_t cap, const int32_t* counts_all, const int32_t* send_tok, const int32_t* send_idx,
+                  const float* send_w, int32_t* tok_rows, const uint64_t* peer_recv_hidden,
+                  const uint64_t* peer_recv_meta, dsmoe_stream_t stream) {
+  if (tokens < 0 || top_k < 1 || top_k > 8 || world < 1 || world > 64 || rank < 0 || rank >= world ||
+      hidden_size <= 0 || hidden_size % 8 || cap < tokens)
+    return fail(DSMOE_ERR_INVALID, "ep_push: bad sizes (tokens %d, cap %d, rank %d of %d)", tokens, cap, rank, world);
+  if (tokens == 0) return DSMOE_OK;
+  const void* ps[8] = {hidden, counts_all, send_tok, send_idx, send_w, tok_rows, peer_recv_hidden, peer_recv_meta};
+  for (const void* p : ps)
+    if (!p) return fail(DSMOE_ERR_INVALID, "ep_push: NULL pointer");
+  if (!aligned16(hidden)) return fail(DSMOE_ERR_INVALID, "ep_push: unaligned rows");
+  DSMOE_CUDA(launch_ep_push(hidden, tokens, hidden_size, top_k, world, rank, cap, counts_all, send_tok, send_idx,
+                            send_w, tok_rows, peer_recv_hidden, peer_recv_meta, reinterpret_cast<cudaStream_t>(stream)));
+  return DSMOE_OK;
+}
+
+int dsmoe_moe_local_peer(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* recv_hidden,
+                         int32_t rows, const int32_t* recv_meta, int32_t world, int32_t rank, int32_t cap,
+                         const uint64_t* peer_return, void* workspace, size_t workspace_bytes, dsmoe_stream_t stream) {
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || cap < 1 || rows < 0 ||
+      static_cast<int64_t>(rows) > static_cast<int64_t>(world) * cap)
+    return fail(DSMOE_ERR_INVALID, "moe_local_peer: bad sizes (rows %d, cap %d, rank %d of %d)", rows, cap, rank,
+                world);
+  if (!recv_meta || !peer_return) return fail(DSMOE_ERR_INVALID, "moe_local_peer: NULL pointer");
+  const int check = check_cfg(cfg);
+  if (check) return check;
+  const size_t cap_rows = static_cast<size_t>(world) * cap;
+  const int K = cfg->top_k;
+  const int32_t* idx = recv_meta;
+  const float* wts = reinterpret_cast<const float*>(recv_meta + cap_rows * K);
+  const int32_t* origin = recv_meta + 2 * cap_rows * K;
+  return moe_local_impl(cfg, w, recv_hidden, rows, idx, wts, nullptr, origin, peer_return, rank, cap, workspace,
+                        workspace_bytes, stream);
+}
+
+size_t dsmoe_ep_meta_bytes(int32_t world, int32_t cap, int32_t top_k) {
+  if (world < 1 || cap < 1 || top_k < 1) return 0;
+  return static_cast<size_t>(world) * cap * (2 * top_k + 2) * sizeof(int32_t);
+}
+
+int dsmoe_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+  if (!dev_ptr || !handle || bytes == 0) return fail(DSMOE_ERR_INVALID, "ipc_alloc: bad arguments");
+  void* p = nullptr;
+  DSMOE_CUDA(cudaMalloc(&p, bytes));
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(DSMOE_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  }
+  memcpy(handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return DSMOE_OK;
+}
+
+int dsmoe_ipc_open(const void* handle, void** dev_ptr) {
+  if (!dev_ptr || !handle) return fail(DSMOE_ERR_INVALID, "ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  DSMOE_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return DSMOE_OK;
+}
+
+int dsmoe_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) return DSMOE_OK;
+  DSMOE_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+  return DSMOE_OK;
+}
+
+int dsmoe_ipc_free(void* dev_ptr) {
+  if (!dev_ptr) return DSMOE_OK;
+  DSMOE_CUDA(cudaFree(dev_ptr));
   return DSMOE_OK;
 }
 

@@ -9,6 +9,10 @@
 // output is bf16(acc): the rank's partial, summed and scaled by the caller.
 // With a residual r (the MoE layer's FFN half, inference/forward.py:109) the
 // output is bf16(r[t] + out[t]): the layer's `hidden + ffn_out` in bf16.
+// With peer outputs (expert parallelism over peer memory) row t is written to
+// the return buffer of the rank it came from, origin[t] = (rank, k), at row
+// me * cap + k of that rank's buffer (peer_out[rank] in this process's
+// address space).
 // This is the reference's arithmetic (inference/forward.py:137,151,153): the
 // fp32 0-dim weight times a bf16 row yields bf16 (the weight is rounded to
 // bf16 by type promotion), the running sum is bf16 and accumulates in top-k
@@ -24,7 +28,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
                                                       const float* __restrict__ w, int top_k,
                                                       const int32_t* __restrict__ row_start, float scale,
                                                       int has_shared, const __nv_bfloat16* __restrict__ residual,
-                                                      __nv_bfloat16* __restrict__ out) {
+                                                      __nv_bfloat16* __restrict__ out,
+                                                      const int32_t* __restrict__ origin,
+                                                      const uint64_t* __restrict__ peer_out, int me, int cap) {
   const int t = blockIdx.x;
   __shared__ int s_row[8];
   __shared__ float s_w[8];
@@ -35,6 +41,11 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
   __syncthreads();
   const int srow = row_start[0] + t;
   const int nchunks = H / 8;
+  __nv_bfloat16* orow = out + static_cast<size_t>(t) * H;
+  if (peer_out) {
+    const int src_rank = origin[2 * t], k = origin[2 * t + 1];
+    orow = reinterpret_cast<__nv_bfloat16*>(peer_out[src_rank]) + (static_cast<size_t>(me) * cap + k) * H;
+  }
   for (int c = threadIdx.x; c < nchunks; c += blockDim.x) {
     // All rows of the token are loaded before the ordered bf16 sum so that
     // the loads overlap.
@@ -74,16 +85,20 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 #pragma unroll
       for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__bfloat162float(rb[i]) + __bfloat162float(ob[i]));
     }
-    reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H)[c] = o;
+    reinterpret_cast<uint4*>(orow)[c] = o;
   }
+  if (peer_out) __threadfence_system();
 }
 }  // namespace cb
 
 cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
                            const int32_t* row_start, float scale, int has_shared, const __nv_bfloat16* residual,
-                           __nv_bfloat16* out, cudaStream_t stream) {
+                           __nv_bfloat16* out, cudaStream_t stream, const int32_t* origin, const uint64_t* peer_out,
+                           int me, int cap) {
   if (T == 0) return cudaSuccess;
-  cb::combine_kernel<<<T, 256, 0, stream>>>(y, T, H, pos, w, top_k, row_start, scale, has_shared, residual, out);
+  cb::combine_kernel<<<T, 256, 0, stream>>>(y, T, H, pos, w, top_k, row_start, scale, has_shared, residual, out,
+                                            origin, peer_out, me, cap);
+
   return cudaGetLastError();
 }
 

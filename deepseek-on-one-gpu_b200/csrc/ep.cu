@@ -120,6 +120,61 @@ __global__ void __launch_bounds__(256) gather_kernel(const __nv_bfloat16* __rest
   }
 }
 
+// Peer-memory dispatch (one kernel instead of a local pack + all-to-all):
+// every send row r of this rank (grouped by destination d, position k inside
+// d's group) is written straight into rank d's receive buffers over NVLink,
+// at row p = (rows that lower ranks send to d) + k, with its routing list and
+// its origin (this rank, k); tok_rows is rewritten to d * cap + k, the row of
+// the partial that d will store back into this rank's return buffer.
+// counts_all[s][d] (all ranks' send counts, gathered beforehand) gives both
+// offsets. Rows are 16-byte vectors; the kernel ends with a system fence.
+__global__ void __launch_bounds__(256) push_kernel(const __nv_bfloat16* __restrict__ x, int H, int K, int W, int me,
+                                                   int cap, const int32_t* __restrict__ counts_all,
+                                                   const int32_t* __restrict__ send_tok,
+                                                   const int32_t* __restrict__ send_idx,
+                                                   const float* __restrict__ send_w, int32_t* __restrict__ tok_rows,
+                                                   const uint64_t* __restrict__ recv_x,
+                                                   const uint64_t* __restrict__ recv_meta) {
+  __shared__ int s_lbase[MAX_WORLD + 1];  // this rank's rows before destination d
+  __shared__ int s_rbase[MAX_WORLD];      // rows lower ranks send to d
+  if (threadIdx.x == 0) {
+    int o = 0;
+    for (int d = 0; d < W; ++d) {
+      s_lbase[d] = o;
+      o += counts_all[me * W + d];
+      int rb = 0;
+      for (int s = 0; s < me; ++s) rb += counts_all[s * W + d];
+      s_rbase[d] = rb;
+    }
+    s_lbase[W] = o;
+  }
+  __syncthreads();
+  const int total = s_lbase[W];
+  const size_t cap_rows = static_cast<size_t>(W) * cap;
+  for (int r = blockIdx.x; r < total; r += gridDim.x) {
+    int d = 0;
+    while (d + 1 < W && s_lbase[d + 1] <= r) ++d;
+    const int k = r - s_lbase[d];
+    const size_t p = static_cast<size_t>(s_rbase[d]) + k;
+    if (k >= cap || p >= cap_rows) continue;  // counts inconsistent with the buffers: write nothing
+    const int t = send_tok[r];
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(recv_x[d]) + p * H);
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = __ldg(src + c);
+    // routing list: idx [W*cap][K] | weights [W*cap][K] | origin [W*cap][2]
+    int32_t* meta = reinterpret_cast<int32_t*>(recv_meta[d]);
+    if (threadIdx.x < K) {
+      meta[p * K + threadIdx.x] = send_idx[static_cast<size_t>(r) * K + threadIdx.x];
+      meta[cap_rows * K + p * K + threadIdx.x] = __float_as_int(send_w[static_cast<size_t>(r) * K + threadIdx.x]);
+    } else if (threadIdx.x == K) {
+      meta[2 * cap_rows * K + p * 2] = me;
+      meta[2 * cap_rows * K + p * 2 + 1] = k;
+      tok_rows[static_cast<size_t>(t) * W + d] = d * cap + k;
+    }
+  }
+  __threadfence_system();
+}
+
 // out[t] = bf16(shared[t] + bf16(scale * acc)), acc = bf16 sum of the
 // returned rows of token t in rank order.
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ part,
@@ -168,6 +223,28 @@ cudaError_t launch_ep_dispatch(const int64_t* idx, const float* w, const void* x
   if (blocks < 1) blocks = 1;
   ep::gather_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), H, send_tok, counts, W,
                                                 static_cast<__nv_bfloat16*>(send_x));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_plan(const int64_t* idx, const float* w, int T, int K, int W, int El, int32_t* counts,
+                           int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx, float* send_w, cudaStream_t stream) {
+  if (W < 1 || W > ep::MAX_WORLD) return cudaErrorInvalidValue;
+  ep::count_kernel<<<W, 1024, 0, stream>>>(idx, T, K, El, counts);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  ep::place_kernel<<<W, 1024, 0, stream>>>(idx, w, T, K, El, W, counts, tok_rows, send_tok, send_idx, send_w);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_push(const void* x, int T, int H, int K, int W, int me, int cap, const int32_t* counts_all,
+                           const int32_t* send_tok, const int32_t* send_idx, const float* send_w, int32_t* tok_rows,
+                           const uint64_t* recv_x, const uint64_t* recv_meta, cudaStream_t stream) {
+  if (W < 1 || W > ep::MAX_WORLD || me < 0 || me >= W || K > 8) return cudaErrorInvalidValue;
+  int blocks = T * (K < W ? K : W);
+  if (blocks > 4096) blocks = 4096;
+  if (blocks < 1) blocks = 1;
+  ep::push_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), H, K, W, me, cap, counts_all,
+                                              send_tok, send_idx, send_w, tok_rows, recv_x, recv_meta);
   return cudaGetLastError();
 }
 

@@ -62,9 +62,11 @@ cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx
 
 // Combine (combine.cu)
 // residual (optional, [T][H]): out = bf16(residual + combined row)
+// peer_out (optional): row t goes to peer_out[origin[2t]] + (me * cap + origin[2t+1]) * H instead of out + t * H
 cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
                            const int32_t* row_start, float scale, int has_shared, const __nv_bfloat16* residual,
-                           __nv_bfloat16* out, cudaStream_t stream);
+                           __nv_bfloat16* out, cudaStream_t stream, const int32_t* origin = nullptr,
+                           const uint64_t* peer_out = nullptr, int me = 0, int cap = 0);
 
 // y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), one row of H per token
 cudaError_t launch_rmsnorm(const void* x, const void* w, float eps, int T, int H, void* y, cudaStream_t stream);
@@ -73,6 +75,11 @@ cudaError_t launch_rmsnorm(const void* x, const void* w, float eps, int T, int H
 cudaError_t launch_ep_dispatch(const int64_t* idx, const float* w, const void* x, int T, int K, int H, int W, int El,
                                int32_t* counts, int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx,
                                float* send_w, void* send_x, cudaStream_t stream);
+cudaError_t launch_ep_plan(const int64_t* idx, const float* w, int T, int K, int W, int El, int32_t* counts,
+                           int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx, float* send_w, cudaStream_t stream);
+cudaError_t launch_ep_push(const void* x, int T, int H, int K, int W, int me, int cap, const int32_t* counts_all,
+                           const int32_t* send_tok, const int32_t* send_idx, const float* send_w, int32_t* tok_rows,
+                           const uint64_t* recv_x, const uint64_t* recv_meta, cudaStream_t stream);
 cudaError_t launch_ep_combine(const void* part, const int32_t* tok_rows, int T, int W, int H, const void* shared,
                               float scale, void* out, cudaStream_t stream);
 

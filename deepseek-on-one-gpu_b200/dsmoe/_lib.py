@@ -24,7 +24,8 @@ EXPORTED = (
     "dsmoe_expert_ffn", "dsmoe_fp8_linear", "dsmoe_read_status", "dsmoe_set_profile_events",
     "dsmoe_expert_ffn_noalloc", "dsmoe_ep_dispatch", "dsmoe_moe_local_workspace_size", "dsmoe_moe_local",
     "dsmoe_ep_combine", "dsmoe_set_gemm_sm_limit", "dsmoe_rms_norm", "dsmoe_moe_layer_ffn_workspace_size",
-    "dsmoe_moe_layer_ffn", "dsmoe_read_ranges",
+    "dsmoe_moe_layer_ffn", "dsmoe_read_ranges", "dsmoe_ep_plan", "dsmoe_ep_push", "dsmoe_moe_local_peer",
+    "dsmoe_ep_meta_bytes", "dsmoe_ipc_alloc", "dsmoe_ipc_open", "dsmoe_ipc_close", "dsmoe_ipc_free",
 )
 
 
@@ -88,6 +89,15 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_moe_layer_ffn_workspace_size.argtypes = [cfgp, i32]
                 L.dsmoe_moe_layer_ffn_workspace_size.restype = sz
                 L.dsmoe_moe_layer_ffn.argtypes = [cfgp, wp, vp, vp, ctypes.c_float, i32, vp, vp, vp, vp, sz, vp]
+                L.dsmoe_ep_plan.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
+                L.dsmoe_ep_push.argtypes = [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]
+                L.dsmoe_moe_local_peer.argtypes = [cfgp, wp, vp, i32, vp, i32, i32, i32, vp, vp, sz, vp]
+                L.dsmoe_ep_meta_bytes.argtypes = [i32, i32, i32]
+                L.dsmoe_ep_meta_bytes.restype = sz
+                L.dsmoe_ipc_alloc.argtypes = [sz, ctypes.POINTER(vp), vp]
+                L.dsmoe_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
+                L.dsmoe_ipc_close.argtypes = [vp]
+                L.dsmoe_ipc_free.argtypes = [vp]
                 u64p = ctypes.POINTER(ctypes.c_uint64)
                 L.dsmoe_read_ranges.argtypes = [i32, ctypes.POINTER(ctypes.c_char_p), u64p, u64p,
                                                 ctypes.POINTER(vp), i32]

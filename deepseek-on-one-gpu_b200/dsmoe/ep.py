@@ -31,8 +31,18 @@ GEMMs). While they overlap an exchange the grouped GEMMs leave ``sm_reserve``
 SMs free (``dsmoe_set_gemm_sm_limit``) so that the collective's kernels are
 not queued behind the persistent GEMM grid. Per token the arithmetic is the
 same in every mode.
+
+Peer-memory exchange (``EPLayer.peer`` set, ``PeerBuffers``): no NCCL
+all-to-all. Every rank maps the other ranks' receive and return buffers
+(CUDA IPC); ``dsmoe_ep_push`` writes each token row straight into its
+destination rank's receive buffer, and the combine of ``dsmoe_moe_local_peer``
+writes each partial row straight into its origin rank's return buffer. Only
+the per-rank counts are gathered (NCCL all-gather of W ints) and two tiny
+all-reduces act as stream-ordered barriers between the writes and the reads.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -79,6 +89,77 @@ class DistExchange:
         self.dist.all_to_all_single(out, send[: sum(send_splits)].contiguous(), output_split_sizes=recv_splits,
                                     input_split_sizes=send_splits, group=self.group)
         return out
+
+
+def _device_view(addr: int, nbytes: int, device) -> torch.Tensor:
+    """A uint8 tensor over ``nbytes`` of device memory at ``addr`` (memory this
+    module owns; the tensor does not free it)."""
+
+    class _Arr:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (addr, False), "version": 3}
+
+    return torch.as_tensor(_Arr(), device=device)
+
+
+class PeerBuffers:
+    """Receive and return buffers of one expert-parallel layer, mapped by every
+    rank of the group: receive rows [world * cap][H] bf16, receive routing
+    metadata (``dsmoe_ep_meta_bytes``), return rows [world * cap][H] bf16.
+    Allocated once (``dsmoe_ipc_alloc``), handles exchanged with an
+    all-gather, peers' buffers mapped with ``dsmoe_ipc_open``; ``tables[name]``
+    holds the W buffer addresses (in this process) on the device."""
+
+    NAMES = ("x", "meta", "back")
+
+    def __init__(self, world: int, rank: int, cap: int, hidden: int, top_k: int, device, group=None):
+        import torch.distributed as dist
+
+        self.world, self.rank, self.cap, self.device = world, rank, cap, torch.device(device)
+        self.nbytes = {"x": world * cap * hidden * 2, "meta": lib().dsmoe_ep_meta_bytes(world, cap, top_k),
+                       "back": world * cap * hidden * 2}
+        self.own, handles = {}, {}
+        with torch.cuda.device(self.device):
+            for name in self.NAMES:
+                ptr_, h = ctypes.c_void_p(), (ctypes.c_char * 64)()
+                check(lib().dsmoe_ipc_alloc(self.nbytes[name], ctypes.byref(ptr_), h), "dsmoe_ipc_alloc")
+                self.own[name] = ptr_.value
+                handles[name] = bytes(h)
+            everyone = [None] * world
+            dist.all_gather_object(everyone, handles, group=group)
+            self.addr = {name: [0] * world for name in self.NAMES}
+            self._opened = []
+            for r in range(world):
+                for name in self.NAMES:
+                    if r == rank:
+                        a = self.own[name]
+                    else:
+                        ptr_ = ctypes.c_void_p()
+                        h = (ctypes.c_char * 64).from_buffer_copy(everyone[r][name])
+                        check(lib().dsmoe_ipc_open(h, ctypes.byref(ptr_)), "dsmoe_ipc_open")
+                        a = ptr_.value
+                        self._opened.append(a)
+                    self.addr[name][r] = a
+        self.tables = {n: torch.tensor(self.addr[n], dtype=torch.int64, device=self.device) for n in self.NAMES}
+        self.views = {n: _device_view(self.own[n], self.nbytes[n], self.device) for n in self.NAMES}
+        self.group = group
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (a collective: every
+        rank calls it, after its last step)."""
+        import torch.distributed as dist
+
+        if not self.own:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for a in self._opened:
+                lib().dsmoe_ipc_close(ctypes.c_void_p(a))
+            dist.barrier(group=self.group)
+            for a in self.own.values():
+                lib().dsmoe_ipc_free(ctypes.c_void_p(a))
+        self.own, self._opened, self.views = {}, [], {}
 
 
 class LocalExchange:
@@ -135,6 +216,8 @@ class EPLayer:
         self.shared = {p: (self.bank.w[p][0], self.bank.s[p][0]) for p in PROJS}
         self._ws = torch.zeros(0, dtype=torch.uint8, device=self.device)
         self._comm = None  # side stream of the overlapped step
+        self.peer: PeerBuffers | None = None  # set by use_peer_memory()
+        self._flag = None
         self.overlap = True  # CUDA tensors: exchange on a side stream, shared expert while rows travel
         self.sm_reserve = 0  # SMs left to the collectives while GEMMs and all-to-alls overlap
 
@@ -211,6 +294,66 @@ class EPLayer:
         """Shared expert on the rank's tokens + sum of the returned partials."""
         return self.combine(self.shared_ffn(x), back, tok_rows)
 
+    def use_peer_memory(self, cap: int, group=None) -> None:
+        """Exchange through mapped peer buffers sized for up to ``cap`` tokens
+        per rank and step (a collective: every rank calls it)."""
+        self.peer = PeerBuffers(self.world, self.rank, cap, self.config.hidden_size, self.config.num_experts_per_tok,
+                                self.device, group)
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
+    def _barrier(self, dev):
+        """Stream-ordered barrier: completes on every rank only after every rank's
+        earlier kernels on its stream have completed."""
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.exchange.dist.all_reduce(self._flag, group=self.exchange.group)
+
+    def _forward_peer(self, x: torch.Tensor) -> torch.Tensor:
+        cfg, pb = self.config, self.peer
+        T, H = x.shape
+        K, W, dev = cfg.num_experts_per_tok, self.world, x.device
+        if T > pb.cap:
+            raise ValueError(f"{T} tokens exceed the peer buffers' capacity of {pb.cap}")
+        idx, w = self.route(x)
+        counts = torch.empty(W, dtype=torch.int32, device=dev)
+        tok_rows = torch.empty(T, W, dtype=torch.int32, device=dev)
+        n_send = max(1, T * min(K, W))
+        send_tok = torch.empty(n_send, dtype=torch.int32, device=dev)
+        send_idx = torch.empty(n_send, K, dtype=torch.int32, device=dev)
+        send_w = torch.empty(n_send, K, dtype=torch.float32, device=dev)
+        stream = stream_handle(dev)
+        check(lib().dsmoe_ep_plan(ptr(idx), ptr(w), T, K, W, self.El, ptr(counts), ptr(tok_rows), ptr(send_tok),
+                                  ptr(send_idx), ptr(send_w), stream), "dsmoe_ep_plan")
+        counts_all = torch.empty(W * W, dtype=torch.int32, device=dev)  # row s: what rank s sends to each rank
+        self.exchange.dist.all_gather_into_tensor(counts_all, counts, group=self.exchange.group)
+        rows = int(counts_all.view(W, W)[:, self.rank].sum().item())  # rows this rank receives
+        check(lib().dsmoe_ep_push(ptr(x), T, K, H, W, self.rank, pb.cap, ptr(counts_all), ptr(send_tok),
+                                  ptr(send_idx), ptr(send_w), ptr(tok_rows), ptr(pb.tables["x"]),
+                                  ptr(pb.tables["meta"]), stream), "dsmoe_ep_push")
+        shared = self.shared_ffn(x)  # independent of the exchange
+        self._barrier(dev)  # every rank's rows have landed
+        if rows:
+            lcfg = _lib.moe_config(self.lcfg)
+            need = lib().dsmoe_moe_local_workspace_size(lcfg, rows)
+            if self._ws.numel() < need:
+                self._ws = torch.zeros(int(need * 1.25) + 4096, dtype=torch.uint8, device=dev)
+            b = self.bank
+            lw = _lib.LayerWeights(
+                gate_weight=None, score_bias=None, n_slots=b.n_slots,
+                w_gate=ptr(b.w["gate_proj"]), s_gate=ptr(b.s["gate_proj"]), w_up=ptr(b.w["up_proj"]),
+                s_up=ptr(b.s["up_proj"]), w_down=ptr(b.w["down_proj"]), s_down=ptr(b.s["down_proj"]),
+                slot_of_expert=ptr(b.slot_of))
+            check(lib().dsmoe_moe_local_peer(lcfg, lw, pb.own["x"], rows, pb.own["meta"], W, self.rank, pb.cap,
+                                             ptr(pb.tables["back"]), ptr(self._ws), self._ws.numel(), stream),
+                  "dsmoe_moe_local_peer")
+        self._barrier(dev)  # every partial is back at its origin
+        back = pb.views["back"].view(torch.bfloat16).view(W * pb.cap, H)
+        return self.combine(shared, back, tok_rows)
+
     def forward(self, x: torch.Tensor, chunks: int = 1) -> torch.Tensor:
         """One expert-parallel MoE step for this rank's tokens ``x`` [T, H] bf16.
         With ``overlap`` (default, CUDA tensors) the exchange runs on a side
@@ -219,6 +362,8 @@ class EPLayer:
         re-reads the rank's expert weights)."""
         shape = x.shape
         x = x.reshape(-1, shape[-1]).contiguous()
+        if self.peer is not None:
+            return self._forward_peer(x).view(shape)
         if self.overlap and x.is_cuda and x.shape[0] >= chunks:
             return self._forward_overlapped(x, chunks).view(shape)
         counts, tok_rows, send_x, meta = self.dispatch(x)

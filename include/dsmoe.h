@@ -235,6 +235,59 @@ DSMOE_API int dsmoe_ep_combine(const void* partials, const int32_t* tok_rows, in
                                dsmoe_stream_t stream);
 
 /*
+ * Expert parallelism over peer memory (no counterpart in the reference; the
+ * exchange without NCCL all-to-all). Every rank allocates, once, receive
+ * buffers for world * cap rows (hidden rows and routing metadata, see
+ * dsmoe_ep_meta_bytes) and a return buffer of world * cap partial rows, in
+ * device memory that the other ranks map (dsmoe_ipc_alloc / dsmoe_ipc_open).
+ * One step on rank `rank` (tokens <= cap):
+ *   1. dsmoe_ep_plan: like dsmoe_ep_dispatch without the row copy (send
+ *      counts, tok_rows, send_tok, send_idx, send_w).
+ *   2. the caller gathers every rank's send_counts into counts_all
+ *      [world][world] (row = sending rank) on every rank.
+ *   3. dsmoe_ep_push: writes each send row straight into the destination
+ *      rank's receive buffers (peer_recv_hidden[d], peer_recv_meta[d]: the
+ *      buffers' addresses in this process) at row
+ *      sum_{s < rank} counts_all[s][d] + k, with its local expert ids,
+ *      weights and origin (rank, k); rewrites tok_rows[t][d] to d * cap + k.
+ *   4. a barrier across ranks (the caller's), then on every rank
+ *      dsmoe_moe_local_peer over its rows received (sum of counts_all[.][rank]):
+ *      the grouped GEMMs of dsmoe_moe_local, whose combine writes each partial
+ *      row into the ORIGIN rank's return buffer (peer_return[s]) at row
+ *      rank * cap + k.
+ *   5. a barrier, then dsmoe_ep_combine over the own return buffer with the
+ *      rewritten tok_rows.
+ * Receive metadata layout (int32): local expert ids [world*cap][top_k],
+ * weights as fp32 bits [world*cap][top_k], origin [world*cap][2].
+ */
+DSMOE_API int dsmoe_ep_plan(const int64_t* topk_idx, const float* topk_w, int32_t tokens, int32_t top_k, int32_t world,
+                            int32_t experts_per_rank, int32_t* send_counts, int32_t* tok_rows, int32_t* send_tok,
+                            int32_t* send_idx, float* send_w, dsmoe_stream_t stream);
+DSMOE_API int dsmoe_ep_push(const void* hidden, int32_t tokens, int32_t top_k, int32_t hidden_size, int32_t world,
+                            int32_t rank, int32_t cap, const int32_t* counts_all, const int32_t* send_tok,
+                            const int32_t* send_idx, const float* send_w, int32_t* tok_rows,
+                            const uint64_t* peer_recv_hidden, const uint64_t* peer_recv_meta, dsmoe_stream_t stream);
+DSMOE_API int dsmoe_moe_local_peer(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* weights,
+                                   const void* recv_hidden, int32_t rows, const int32_t* recv_meta, int32_t world,
+                                   int32_t rank, int32_t cap, const uint64_t* peer_return, void* workspace,
+                                   size_t workspace_bytes, dsmoe_stream_t stream);
+DSMOE_API size_t dsmoe_ep_meta_bytes(int32_t world, int32_t cap, int32_t top_k);
+
+/*
+ * Device memory other processes on this node can map (CUDA IPC; used for
+ * the peer-memory exchange buffers). dsmoe_ipc_alloc allocates `bytes` and
+ * writes a DSMOE_IPC_HANDLE_BYTES handle; another process maps it with
+ * dsmoe_ipc_open (not in the allocating process itself) and unmaps it with
+ * dsmoe_ipc_close; the owner releases it with dsmoe_ipc_free. These allocate:
+ * call them at set-up, not per step.
+ */
+#define DSMOE_IPC_HANDLE_BYTES 64
+DSMOE_API int dsmoe_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+DSMOE_API int dsmoe_ipc_open(const void* handle, void** dev_ptr);
+DSMOE_API int dsmoe_ipc_close(void* dev_ptr);
+DSMOE_API int dsmoe_ipc_free(void* dev_ptr);
+
+/*
  * Allocation-free variant of dsmoe_expert_ffn (no counterpart in the
  * reference; an addition of this library).
  *

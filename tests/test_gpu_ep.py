@@ -100,3 +100,40 @@ def test_ep_overlapped_two_stream_step(chunks, reserve):
     idx, w = O.route_ref(x.cpu(), L.gate)
     ref = O.moe_block_grouped(x.cpu(), idx, w, L.expert, L.shared())
     assert O.rel_rms(ov.float().cpu(), ref.float()) < REL_RMS_TOL
+
+
+def test_ep_peer_memory_one_rank_group():
+    """The peer-memory exchange (rows pushed into mapped receive buffers,
+    partials written back into the origin's return buffer, tiny NCCL
+    barriers) on a one-rank NCCL group gives the all-to-all step's output
+    bit for bit."""
+    import socket
+
+    import torch.distributed as dist
+
+    from dsmoe.ep import DistExchange
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1, device_id=DEV)
+    try:
+        H, F = 512, 256
+        cfg = DeepSeekConfig(hidden_size=H, moe_intermediate_size=F)
+        store = SyntheticWeightStore(cfg, seed=81, device=DEV, pin_memory=False, gen_device="cpu")
+        layer = EPLayer(cfg, store, DEV, 2, 1, 0, exchange=DistExchange(), expert_source=store.device_expert)
+        xs = [activations(82 + i, T, H).to(DEV) for i, T in enumerate((100, 1, 37))]
+        plain = [layer.forward(x) for x in xs]
+        layer.use_peer_memory(cap=128)
+        try:
+            peer = [layer.forward(x) for x in xs]
+            torch.cuda.synchronize()
+            for a, b in zip(plain, peer):
+                assert torch.equal(a, b)
+            with pytest.raises(ValueError):
+                layer.forward(activations(90, 129, H).to(DEV))
+        finally:
+            layer.close()
+    finally:
+        dist.destroy_process_group()

@@ -52,6 +52,19 @@ def _rank_main(rank, world, port, q):
             out = layer.forward(x, chunks=chunks)
             single = moe_block(x, 3, store, gt, cfg)
             results.append(rel_rms(out.float().cpu(), single.float().cpu()))
+        # the same steps through the peer-memory exchange: bit-identical outputs
+        ref = []
+        for step, T in enumerate((64, 200, 1)):
+            x = activations(500 + step + 10 * rank, T, 512).to(dev)
+            layer.overlap, layer.sm_reserve = False, 0
+            ref.append((x, layer.forward(x)))
+        layer.use_peer_memory(cap=256)
+        try:
+            for x, want in ref:
+                got = layer.forward(x)
+                results.append(0.0 if torch.equal(got, want) else 1.0)
+        finally:
+            layer.close()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, results))
