@@ -315,8 +315,8 @@ def main():
                     help="expert-parallel step: token chunks whose all-to-alls overlap the expert GEMMs (1 = none)")
     ap.add_argument("--sm-reserve", type=int, default=0,
                     help="expert-parallel step: SMs the grouped GEMMs leave to the all-to-alls while they overlap")
-    ap.add_argument("--peer", action="store_true",
-                    help="expert-parallel step: exchange rows through mapped peer buffers (no NCCL all-to-all)")
+    ap.add_argument("--nccl-exchange", action="store_true",
+                    help="expert-parallel step: NCCL all-to-all instead of the default peer-memory exchange")
     ap.add_argument("--no-overlap", action="store_true",
                     help="expert-parallel step: exchange and GEMMs in one stream, one after the other")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
@@ -373,7 +373,7 @@ def main():
                            expert_source=store.device_expert)
         ep_layer.sm_reserve = args.sm_reserve
         ep_layer.overlap = not args.no_overlap
-        if args.peer:
+        if not args.nccl_exchange:
             ep_layer.use_peer_memory(cap=T)
         bank = None
         x = activations(1000 * seed + rank, T, H, device=dev)
@@ -647,7 +647,8 @@ def main():
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) FP8 block-quantised experts)",
             "config": {"workload": (f"1 DeepSeek-R1 MoE layer, expert-parallel over {world} GPUs "
                                     f"({cfg.n_routed_experts // world} experts per GPU, gate and shared expert "
-                                    f"replicated), T={T} tokens per GPU, NCCL all-to-all dispatch/combine "
+                                    f"replicated), T={T} tokens per GPU, "
+                                    f"{'NCCL all-to-all' if args.nccl_exchange else 'peer-memory'} dispatch/combine "
                                     f"(config {args.config})")
                                    if ep else
                                    (f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, "
@@ -658,7 +659,7 @@ def main():
                        "hottest_expert_over_mean": hottest_over_mean,
                        "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
                        "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU",
-                       **({"ep_exchange": "peer memory (IPC-mapped buffers)" if args.peer else "NCCL all-to-all",
+                       **({"ep_exchange": "NCCL all-to-all" if args.nccl_exchange else "peer memory (IPC-mapped buffers)",
                             "ep_overlap": not args.no_overlap, "ep_chunks": args.chunks,
                             "ep_sm_reserve": args.sm_reserve} if ep else {})},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
