@@ -238,6 +238,19 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 
 
 // --------------------------------------------------------------- numerics
+// (a0, a1) = (p0 * s + a0, p1 * s + a1) in one packed fp32x2 FMA; each lane
+// is a fused multiply-add rounded to nearest, exactly like fmaf.
+__device__ __forceinline__ void fma2(float& a0, float& a1, float p0, float p1, float s) {
+  asm("{\n\t.reg .b64 pa, ps, pc;\n\t"
+      "mov.b64 pa, {%2, %3};\n\t"
+      "mov.b64 ps, {%4, %4};\n\t"
+      "mov.b64 pc, {%0, %1};\n\t"
+      "fma.rn.f32x2 pc, pa, ps, pc;\n\t"
+      "mov.b64 {%0, %1}, pc;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(p0), "f"(p1), "f"(s));
+}
+
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }

@@ -190,7 +190,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         const int col0 = nt * BN;
         const int ncols = min(BN, s_counts[g] - col0);
         const int nsub = (ncols + SUB - 1) / SUB;
-        const bool small = BN == SUB || (nsub * SUB < BN && nsub <= 2);  // a few 32-row boxes beat one big box
+        // A few 32-row boxes beat one big box; four or more cost more than the
+        // rows they save (a 128-token tile as 4 boxes: +8% kernel time).
+        const bool small = BN == SUB || (nsub * SUB < BN && nsub <= 2);
         const int row0 = s_rows[g] + col0;
         const int wrow = slot * p.M + (mt - mat * mt_per_mat) * BM;
         const uint32_t bytes = BM * BK + 2 * (small ? nsub * SUB : BN) * BK;
@@ -335,8 +337,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
             } else {
               tmem_ld_wait();
             }
+            // Packed fp32x2 FMAs: half the issue slots of scalar fmaf, same
+            // rounding (-2% kernel time at T=4096, where the GEMM runs at
+            // the power cap).
 #pragma unroll
-            for (int i = 0; i < CHUNK; ++i) acc[q * CHUNK + i] = fmaf(part[i], sw, acc[q * CHUNK + i]);
+            for (int i = 0; i < CHUNK; i += 2)
+              fma2(acc[q * CHUNK + i], acc[q * CHUNK + i + 1], part[i], part[i + 1], sw);
           }
         }
         tc_fence_before();
