@@ -96,6 +96,32 @@ def expert_load_rates(cfg, dev, n_experts: int = 16, layer: int = 7) -> dict:
     return out
 
 
+def _torch_sort_sample(logits, temperature: float, top_p: float):
+    """The reference's sampling steps (softmax, full sort, cumsum, mask,
+    renormalise, multinomial, gather) as plain torch ops on the GPU: the
+    comparison point for the device sampler."""
+    probs = torch.softmax(logits / temperature, dim=-1)
+    sp, si = probs.sort(dim=-1, descending=True)
+    cum = sp.cumsum(dim=-1)
+    sp[cum - sp > top_p] = 0.0
+    sp /= sp.sum(dim=-1, keepdim=True)
+    return si.gather(-1, torch.multinomial(sp, num_samples=1)).squeeze(-1)
+
+
+def sampler_rates(dev, dev_ms) -> dict:
+    """Next-token sampling at DeepSeek's vocabulary (129,280 fp32 logits per
+    row, T = 0.6, top_p = 0.9): the device sampler (dsmoe.sample) against the
+    reference's steps as torch ops, device-timed per call, for 1 and 64 rows."""
+    from dsmoe import sample
+    from dsmoe.synthetic import logits as make_logits
+    out = {}
+    for B in (1, 64):
+        x = make_logits(40, B, 129280, 3.0, dev)
+        out[f"sampler_us_b{B}"] = 1e3 * dev_ms(lambda: sample(x, 0.6, 0.9), n=50)
+        out[f"torch_sort_sampler_us_b{B}"] = 1e3 * dev_ms(lambda: _torch_sort_sample(x, 0.6, 0.9), n=50)
+    return out
+
+
 def peaks():
     """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     try:
@@ -613,10 +639,11 @@ def main():
         dn_ms = dev_ms(lambda: dense_ffn(x, dense_w))
         dense_bytes = 3 * 18432 * H + T * H * 2 * 2
         loader = expert_load_rates(cfg, dev)
+        sampler = sampler_rates(dev, dev_ms)
         widened = {"rms_norm_ms": norm_ms, "rms_norm_GB_s": 2 * T * H * 2 / (norm_ms / 1e3) / 1e9,
                    "moe_layer_ffn_ms": ffn_ms, "moe_layer_ffn_over_block": ffn_ms / ms_max,
                    "dense_ffn_ms": dn_ms, "dense_ffn_tflops": 2.0 * T * 3 * 18432 * H / (dn_ms / 1e3) / 1e12,
-                   "dense_ffn_weight_GB": dense_bytes / 1e9, **loader}
+                   "dense_ffn_weight_GB": dense_bytes / 1e9, **loader, **sampler}
         del dense_w
     status = Workspace.get(dev).status()
 

@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -443,6 +444,27 @@ int dsmoe_rms_norm(const void* x, const void* weight, float eps, int32_t tokens,
   if (!x || !weight || !out || !aligned16(x) || !aligned16(weight) || !aligned16(out))
     return fail(DSMOE_ERR_INVALID, "x / weight / out NULL or not 16-byte aligned");
   DSMOE_CUDA(launch_rmsnorm(x, weight, eps, tokens, hidden, out, reinterpret_cast<cudaStream_t>(stream)));
+  return DSMOE_OK;
+}
+
+int dsmoe_sample_top_p(const float* logits, int32_t rows, int32_t vocab, int64_t row_stride, float temperature,
+                       float top_p, const float* uniforms, int64_t* tokens, int32_t* nucleus_sizes,
+                       dsmoe_stream_t stream) {
+  if (rows < 0 || rows > 65535) return fail(DSMOE_ERR_INVALID, "0 <= rows <= 65535");
+  if (vocab < 1 || vocab > top_p_max_vocab())
+    return fail(DSMOE_ERR_UNSUPPORTED, "vocab %d outside [1, %d]", vocab, top_p_max_vocab());
+  if (row_stride < vocab) return fail(DSMOE_ERR_INVALID, "row_stride < vocab");
+  if (!(temperature >= 0.f) || !std::isfinite(temperature))
+    return fail(DSMOE_ERR_INVALID, "temperature must be finite and >= 0");
+  if (!(top_p >= 0.f)) return fail(DSMOE_ERR_INVALID, "top_p must be >= 0");
+  if (rows == 0) return DSMOE_OK;
+  if (!logits || !tokens || (temperature > 0.f && !uniforms))
+    return fail(DSMOE_ERR_INVALID, "logits / tokens NULL, or uniforms NULL with temperature > 0");
+  if (reinterpret_cast<uintptr_t>(logits) % 4 || reinterpret_cast<uintptr_t>(tokens) % 8)
+    return fail(DSMOE_ERR_INVALID, "logits / tokens misaligned");
+  DSMOE_CUDA(launch_top_p(logits, rows, vocab, row_stride, temperature, top_p, uniforms,
+                          reinterpret_cast<long long*>(tokens), nucleus_sizes,
+                          reinterpret_cast<cudaStream_t>(stream)));
   return DSMOE_OK;
 }
 

@@ -71,6 +71,11 @@ cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* 
 // y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), one row of H per token
 cudaError_t launch_rmsnorm(const void* x, const void* w, float eps, int T, int H, void* y, cudaStream_t stream);
 
+// Temperature + top-p sampling (sampler.cu), one cluster per row
+int top_p_max_vocab();
+cudaError_t launch_top_p(const float* logits, int rows, int V, long long ld, float temperature, float top_p,
+                         const float* uniforms, long long* tokens, int* nucleus, cudaStream_t stream);
+
 // Expert parallelism (ep.cu)
 cudaError_t launch_ep_dispatch(const int64_t* idx, const float* w, const void* x, int T, int K, int H, int W, int El,
                                int32_t* counts, int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx,

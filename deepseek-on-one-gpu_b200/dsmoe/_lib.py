@@ -26,6 +26,7 @@ EXPORTED = (
     "dsmoe_ep_combine", "dsmoe_set_gemm_sm_limit", "dsmoe_rms_norm", "dsmoe_moe_layer_ffn_workspace_size",
     "dsmoe_moe_layer_ffn", "dsmoe_read_ranges", "dsmoe_ep_plan", "dsmoe_ep_push", "dsmoe_moe_local_peer",
     "dsmoe_ep_meta_bytes", "dsmoe_ipc_alloc", "dsmoe_ipc_open", "dsmoe_ipc_close", "dsmoe_ipc_free",
+    "dsmoe_sample_top_p",
 )
 
 
@@ -98,6 +99,8 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
                 L.dsmoe_ipc_close.argtypes = [vp]
                 L.dsmoe_ipc_free.argtypes = [vp]
+                L.dsmoe_sample_top_p.argtypes = [vp, i32, i32, ctypes.c_int64, ctypes.c_float, ctypes.c_float, vp, vp,
+                                                 vp, vp]
                 u64p = ctypes.POINTER(ctypes.c_uint64)
                 L.dsmoe_read_ranges.argtypes = [i32, ctypes.POINTER(ctypes.c_char_p), u64p, u64p,
                                                 ctypes.POINTER(vp), i32]

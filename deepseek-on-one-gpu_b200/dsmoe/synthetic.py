@@ -112,6 +112,19 @@ def norm_weight(seed: int, layer: int, which: int, hidden: int, device="cpu", st
     return (1.0 + torch.randn(hidden, generator=g, dtype=torch.float32) * std).to(torch.bfloat16).to(device)
 
 
+def logits(seed: int, rows: int, vocab: int, scale: float, device="cpu") -> torch.Tensor:
+    """Next-token logits ``[rows, vocab]`` fp32 ~ N(0, scale^2): larger
+    ``scale`` gives a more peaked softmax (smaller nucleus)."""
+    g = _gen("cpu", seed, 5, 17)
+    return torch.randn(rows, vocab, generator=g, dtype=torch.float32).mul_(scale).to(device)
+
+
+def uniforms(seed: int, rows: int, device="cpu") -> torch.Tensor:
+    """One uniform in [0, 1) per row (the sampler's draw)."""
+    g = _gen("cpu", seed, 5, 19)
+    return torch.rand(rows, generator=g, dtype=torch.float32).to(device)
+
+
 class SyntheticLayer:
     """Lazily generated weights of one MoE layer (per-expert cache optional)."""
 

@@ -320,6 +320,32 @@ DSMOE_API int dsmoe_expert_ffn_noalloc(const void* x, int32_t tokens, int32_t hi
                                        const void* w_gate, const float* s_gate, const void* w_up, const float* s_up,
                                        const void* w_down, const float* s_down, void* out, dsmoe_stream_t stream);
 
+/*
+ * Next-token sampling, replaces `sample` (inference/engine.py:166-190) and
+ * the .item() read of the decode loop (engine.py:116-117, 142-151): the token
+ * ids stay on the device.
+ *   logits    [rows][row_stride] fp32 (vocab used per row, 1 <= vocab <= 131072)
+ *   temperature == 0: tokens[r] = first index of the row maximum (argmax);
+ *   temperature > 0:  softmax(logits / temperature), keep the shortest
+ *     descending prefix whose preceding mass stays <= top_p (the reference's
+ *     mask `cumulative - p > top_p`), and take the element where the
+ *     descending running mass of the kept set first exceeds
+ *     uniforms[r] * (kept mass) (inverse CDF with a caller-drawn uniform in
+ *     [0, 1); the reference draws it inside torch.multinomial).
+ *   tokens        [rows] int64 output; -1 for a row whose maximum logit is not
+ *                 finite (the reference's softmax is NaN there)
+ *   nucleus_sizes [rows] int32 output (NULL allowed): kept elements per row
+ * Equal logits are ordered by index. Masses are exact integers
+ * (round(2^40 * exp(l/T - max/T))), so results are deterministic; they can
+ * differ from the reference's fp32 cumsum where a boundary lies within
+ * ~1e-6 of top_p or of the drawn uniform. One cluster of up to 8 CTAs per row.
+ * rows <= 65535; temperature >= 0 and finite; top_p >= 0 (>= 1 keeps all);
+ * uniforms may be NULL when temperature == 0.
+ */
+DSMOE_API int dsmoe_sample_top_p(const float* logits, int32_t rows, int32_t vocab, int64_t row_stride,
+                                 float temperature, float top_p, const float* uniforms, int64_t* tokens,
+                                 int32_t* nucleus_sizes, dsmoe_stream_t stream);
+
 /* Reads (synchronously) and clears the device error word kept in `workspace`. */
 DSMOE_API int dsmoe_read_status(void* workspace, int32_t* device_status, dsmoe_stream_t stream);
 

@@ -31,7 +31,7 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO / "deepseek-on-one-gpu_b200"))
 
-from dsmoe.synthetic import SyntheticLayer, activations, norm_weight  # noqa: E402
+from dsmoe.synthetic import SyntheticLayer, activations, logits, norm_weight, uniforms  # noqa: E402
 
 # name: (seed, T, H, F, E, kind)
 CASES = {
@@ -43,6 +43,16 @@ CASES = {
     "ffn_t16": (103, 16, 512, 256, 256, "layer_ffn"),
     "ffn_c1_t8_full": (0, 8, 7168, 2048, 256, "layer_ffn"),
     "norm_t16_full": (104, 16, 7168, 2048, 256, "norm"),
+}
+# Next-token sampling (inference/engine.py:166-190):
+# name: (seed, rows, vocab, logit scale, temperature, top_p)
+SAMPLE_CASES = {
+    "sample_v1000": (200, 8, 1000, 2.0, 0.6, 0.9),
+    "sample_v129280": (201, 2, 129280, 3.0, 0.6, 0.9),
+    "sample_topp_small": (202, 8, 4096, 1.0, 1.0, 0.05),
+    "sample_greedy": (203, 4, 129280, 3.0, 0.0, 0.9),
+    "sample_topp1": (204, 4, 2000, 1.5, 0.8, 1.0),
+    "sample_hot": (205, 4, 32000, 8.0, 0.3, 0.95),
 }
 EPS = 1e-6
 LAYER = 3
@@ -78,8 +88,11 @@ def main(ref_root: str) -> None:
     from inference.config import DeepSeekConfig as RefConfig  # noqa: E402
 
     torch.set_num_threads(os.cpu_count() or 1)
-    only = sys.argv[2:] or list(CASES)
+    only = sys.argv[2:] or list(CASES) + list(SAMPLE_CASES)
     for name in only:
+        if name in SAMPLE_CASES:
+            make_sample_case(name)
+            continue
         seed, T, H, F, E, kind = CASES[name]
         t0 = time.time()
         cfg = RefConfig(hidden_size=H, moe_intermediate_size=F, n_routed_experts=E)
@@ -107,6 +120,33 @@ def main(ref_root: str) -> None:
             rec["out"] = out.reshape(T, H).clone()
         torch.save(rec, HERE / f"{name}.pt")
         print(f"{name}: {time.time() - t0:.1f}s", flush=True)
+
+
+def make_sample_case(name: str) -> None:
+    sys.path.insert(0, str(REPO))
+    from inference import engine as ref_engine  # noqa: E402
+    from oracle.sampler import inverse_cdf  # noqa: E402
+
+    seed, B, V, scale, temperature, top_p = SAMPLE_CASES[name]
+    x = logits(seed, B, V, scale)
+    u = uniforms(seed, B)
+    seen = {}
+
+    def draw(probs, num_samples, *args, **kwargs):
+        seen["kept"] = (probs > 0).sum(dim=-1)
+        return inverse_cdf(probs, u)[:, None]
+
+    real = torch.multinomial
+    torch.multinomial = draw
+    try:
+        tokens = ref_engine.sample(x.clone(), temperature, top_p)
+    finally:
+        torch.multinomial = real
+    kept = seen.get("kept", torch.ones(B, dtype=torch.int64))
+    rec = dict(seed=seed, rows=B, vocab=V, scale=scale, temperature=temperature, top_p=top_p, u=u.clone(),
+               tokens=tokens.reshape(B).clone(), nucleus=kept.reshape(B).clone(), torch_version=str(torch.__version__))
+    torch.save(rec, HERE / f"{name}.pt")
+    print(f"{name}: tokens {rec['tokens'].tolist()} nucleus {rec['nucleus'].tolist()}", flush=True)
 
 
 if __name__ == "__main__":

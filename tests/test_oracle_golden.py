@@ -109,3 +109,41 @@ def test_layer_ffn_close(name):
     out = O.moe_layer_ffn(x, norm_weight(g["seed"], g["layer"], 1, g["H"]), g["eps"], layer.gate, layer.expert,
                           layer.shared())
     assert O.rel_rms(out, g["out"]) < 1e-3
+
+
+SAMPLE_CASES = ["sample_v1000", "sample_v129280", "sample_topp_small", "sample_greedy", "sample_topp1", "sample_hot"]
+
+
+@pytest.mark.parametrize("name", SAMPLE_CASES)
+def test_sampler_matches_reference_exactly(name):
+    """oracle/sampler.py against the reference's own sample() (run with the
+    same explicit draw): same tokens, same nucleus sizes."""
+    from dsmoe.synthetic import logits
+    from oracle import sampler as S
+    g = load(name)
+    x = logits(g["seed"], g["rows"], g["vocab"], g["scale"])
+    tokens, nucleus = S.sample_top_p(x, g["temperature"], g["top_p"], g["u"])
+    assert torch.equal(tokens, g["tokens"])
+    if g["temperature"] != 0:
+        assert torch.equal(nucleus, g["nucleus"])
+
+
+def test_sampler_oracle_properties():
+    """Small cases worked by hand: the nucleus rule and the explicit draw."""
+    from oracle import sampler as S
+    # probabilities 0.5, 0.3, 0.2 (logits = log p, T = 1)
+    x = torch.log(torch.tensor([[0.2, 0.5, 0.3]]))
+    for top_p, kept in ((0.0, 1), (0.49, 1), (0.5, 2), (0.79, 2), (0.81, 3), (1.0, 3)):
+        _, n = S.sample_top_p(x, 1.0, top_p, torch.tensor([0.0]))
+        assert int(n) == kept, (top_p, int(n))
+    # all kept: u below 0.5 -> index 1, [0.5, 0.8) -> index 2, above -> index 0
+    for u, tok in ((0.0, 1), (0.49, 1), (0.51, 2), (0.79, 2), (0.81, 0), (0.999, 0)):
+        t, _ = S.sample_top_p(x, 1.0, 1.0, torch.tensor([u]))
+        assert int(t) == tok, (u, int(t))
+    # top 2 kept (mass 0.8): renormalised 0.625 / 0.375
+    for u, tok in ((0.6, 1), (0.63, 2)):
+        t, _ = S.sample_top_p(x, 1.0, 0.5, torch.tensor([u]))
+        assert int(t) == tok, (u, int(t))
+    # temperature 0: argmax, first of equal maxima
+    t, _ = S.sample_top_p(torch.tensor([[1.0, 3.0, 3.0, 2.0]]), 0.0, 0.9, None)
+    assert int(t) == 1
