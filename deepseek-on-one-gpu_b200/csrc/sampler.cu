@@ -5,7 +5,7 @@
 // sort of the 129,280 probabilities, cumsum, mask every position whose
 // preceding mass exceeds top_p, renormalise, torch.multinomial, then
 // .item() to read the token back. This kernel does the same selection with
-// no sort and no host round trip:
+// no full sort and no host round trip:
 //
 //   * one thread-block cluster per row; CTA c of the cluster holds logits
 //     [c * 16384, (c + 1) * 16384) of the row in registers (16 order keys
@@ -17,14 +17,20 @@
 //     e = exp(l / T - max / T); sums of masses are exact and independent of
 //     the summation order, so every decision below is deterministic and
 //     identical in all CTAs of the cluster;
-//   * "the first position, in descending order, where the running mass
-//     exceeds a target" is found by a radix select over the keys: four
-//     passes of 8-bit digits, each a cluster-wide histogram of (mass, count)
-//     per digit (warp-aggregated shared-memory atomics, the CTAs' histograms
-//     summed through distributed shared memory), then a scan from the top
-//     digit. Run with target floor(top_p * Q) it finds the last element of
-//     the nucleus (the reference keeps a position iff the mass before it is
-//     <= top_p); run with target floor(u * kept mass) it finds the sampled
+//   * "the first element, in descending order, where the running mass
+//     exceeds a target" is found in two levels. First a cluster-wide
+//     histogram of (mass, count) over 1024 buckets of (max - l) / T (equal
+//     widths over the 28.5 units in which an element has non-zero mass),
+//     built once per row and scanned from the top bucket, gives the bucket
+//     that crosses the target. Then the keys of that bucket (a few hundred
+//     for real or random logits) are gathered from all CTAs through
+//     distributed shared memory and every CTA finishes on them alone, with a
+//     4-pass 8-bit radix select in its own shared memory. A bucket of more
+//     than 4096 elements (rows of many equal logits) is resolved instead by
+//     cluster-wide radix passes restricted to the bucket.
+//   * With target floor(top_p * Q) this finds the last element of the
+//     nucleus (the reference keeps a position iff the mass before it is
+//     <= top_p); with target floor(u * kept mass) it finds the sampled
 //     element (inverse CDF in descending order, the order the reference's
 //     multinomial indexes).
 //   * equal logits are ordered by vocabulary index (a stable sort); the
@@ -48,17 +54,39 @@ constexpr int THREADS = 1024;
 constexpr int WARPS = THREADS / 32;
 constexpr int EPT = 16;                 // logits per thread
 constexpr int CHUNK = THREADS * EPT;    // logits per CTA
-constexpr int RADIX = 256;
+constexpr int MAX_CTAS = 8;             // CTAs per cluster (one row)
+constexpr int RADIX = 256;              // digits of a key radix pass
+constexpr int NCOPY = 8;                // histogram copies of a cluster radix pass (warp w -> copy w % NCOPY)
+constexpr int VB = 1024;                // value buckets of the first level (one per thread)
+constexpr int VCOPY = 4;                // copies of the value histogram
+constexpr int CAP = 4096;               // keys a bucket may hold to be finished locally
 constexpr float kMassScale = 1099511627776.0f;  // 2^40
+// e = exp(x) has a non-zero mass round(e * 2^40) iff x > -28.42; buckets span 28.5
+constexpr float kBucketScale = static_cast<float>(VB) / 28.5f;
+static_assert(VB == THREADS, "one value bucket per thread");
 
 struct Shared {
-  unsigned long long hmass[3][RADIX];  // [0]: first-digit histogram (kept), [1], [2]: later passes, alternating
-  unsigned int hcount[3][RADIX];
-  unsigned long long scan_m[RADIX];    // cluster totals per digit, descending digit order, then scanned
-  unsigned int scan_n[RADIX];
+  // first level: value buckets (this CTA's histogram is read by the cluster)
+  unsigned long long vpm[VCOPY][VB];
+  unsigned int vpc[VCOPY][VB];
+  unsigned long long vmass[VB];
+  unsigned int vcount[VB];
+  // second level: the crossing bucket's keys; one list per select (this
+  // CTA's, read by the cluster) and the merged list of the whole cluster
+  uint32_t cand[2][CAP];
+  uint32_t merged[CAP];
+  unsigned int cand_n[2];
+  // key radix passes (local finish, and the cluster fallback)
+  unsigned long long pm[NCOPY][RADIX];
+  unsigned int pc[NCOPY][RADIX];
+  unsigned long long hmass[2][RADIX];  // cluster fallback: this CTA's histogram, alternating
+  unsigned int hcount[2][RADIX];
+  // block scans and reductions
+  unsigned long long scan_m[VB];
+  unsigned int scan_n[VB];
   unsigned long long warp64[WARPS];
   unsigned int warp32[WARPS];
-  unsigned long long cta_max;          // read by the other CTAs of the cluster
+  unsigned long long cta_max;  // read by the other CTAs of the cluster
   unsigned long long cta_mass;
   unsigned int cta_ties;
 };
@@ -79,15 +107,27 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 constexpr uint32_t kNoKey = 0u;
 constexpr uint32_t kNaNKey = 0xffffffffu;
 
-// Integer mass of a logit: round(2^40 * exp(l / T - max / T)), 0 past the
-// end of the row. Written with explicitly rounded operations so that every
-// evaluation, wherever it is inlined, gives the same bits.
-__device__ __forceinline__ unsigned long long mass_of(uint32_t key, float temperature, float mt) {
-  if (key == kNoKey) return 0ull;
-  const float x = __fsub_rn(__fdiv_rn(key_value(key), temperature), mt);
-  return __float2ull_rn(__fmul_rn(expf(x), kMassScale));
+// x - max(x) for x = l / T, written with explicitly rounded operations so that
+// every evaluation, wherever it is inlined, gives the same bits.
+__device__ __forceinline__ float rel_x(uint32_t key, float temperature, float mt) {
+  return __fsub_rn(__fdiv_rn(key_value(key), temperature), mt);
 }
 
+// Integer mass of a logit: round(2^40 * exp(l / T - max / T)), 0 past the end
+// of the row.
+__device__ __forceinline__ unsigned long long mass_of(uint32_t key, float temperature, float mt) {
+  if (key == kNoKey) return 0ull;
+  return __float2ull_rn(__fmul_rn(expf(rel_x(key, temperature, mt)), kMassScale));
+}
+
+// First-level bucket: 0 holds the largest logits; monotone in the key.
+__device__ __forceinline__ int vbucket(uint32_t key, float temperature, float mt) {
+  const float d = __fmul_rn(-rel_x(key, temperature, mt), kBucketScale);  // >= 0
+  return d >= static_cast<float>(VB - 1) ? VB - 1 : static_cast<int>(d);
+}
+
+// Block-wide sum (kMax = false) or max of a 64-bit value; every thread gets
+// the result.
 template <bool kMax>
 __device__ __forceinline__ unsigned long long block_reduce(unsigned long long v, unsigned long long* scratch) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -133,34 +173,35 @@ __device__ __forceinline__ unsigned block_excl_scan(unsigned v, unsigned* scratc
   return warp_excl + incl - v;
 }
 
+// Sum of q over the lanes of `grp` (q <= 2^40, summed as two 20-bit halves:
+// 32 lanes of 2^20 fit 32 bits); called by exactly the lanes of grp.
+__device__ __forceinline__ unsigned long long group_sum(unsigned grp, unsigned long long q) {
+  const unsigned lo = __reduce_add_sync(grp, static_cast<unsigned>(q & 0xfffffu));
+  const unsigned hi = __reduce_add_sync(grp, static_cast<unsigned>(q >> 20));
+  return (static_cast<unsigned long long>(hi) << 20) + lo;
+}
+
+// True (in every lane) when all lanes with `pred` share the digit `d`.
+__device__ __forceinline__ bool warp_uniform(unsigned act, bool pred, uint32_t d) {
+  const uint32_t d0 = __shfl_sync(0xffffffffu, d, __ffs(act) - 1);
+  return __all_sync(0xffffffffu, !pred || d == d0);
+}
+
 // Adds (mass q, count 1) to digit `d` of the histogram for every lane with
 // `pred`; lanes of a warp that share a digit are summed first, so one atomic
-// per (warp, digit). q <= 2^40 is summed as two 20-bit halves (32 lanes of
-// 2^20 fit 32 bits).
+// per (warp, digit). Every lane of the warp must call it.
 __device__ __forceinline__ void hist_add(bool pred, uint32_t d, unsigned long long q, unsigned long long* hm,
                                          unsigned* hc) {
   const unsigned act = __ballot_sync(0xffffffffu, pred);
+  if (!act) return;  // warp-uniform
+  const bool uni = warp_uniform(act, pred, d);
   if (pred) {
-    const unsigned grp = __match_any_sync(act, d);
-    const unsigned lo = __reduce_add_sync(grp, static_cast<unsigned>(q & 0xfffffu));
-    const unsigned hi = __reduce_add_sync(grp, static_cast<unsigned>(q >> 20));
+    const unsigned grp = uni ? act : __match_any_sync(act, d);
+    const unsigned long long sum = group_sum(grp, q);
     if ((threadIdx.x & 31) == static_cast<unsigned>(__ffs(grp) - 1)) {
-      atomicAdd(&hm[d], (static_cast<unsigned long long>(hi) << 20) + lo);
+      atomicAdd(&hm[d], sum);
       atomicAdd(&hc[d], static_cast<unsigned>(__popc(grp)));
     }
-  }
-}
-
-// Histogram of the digit at `shift` over the elements with mass whose key
-// matches `prefix` on the bits of `pmask` (the mass is only evaluated for
-// matching elements).
-__device__ __forceinline__ void accumulate(const uint32_t* key, float temperature, float mt, uint32_t prefix,
-                                           uint32_t pmask, int shift, unsigned long long* hm, unsigned* hc) {
-#pragma unroll
-  for (int i = 0; i < EPT; ++i) {
-    const bool match = (key[i] & pmask) == prefix;
-    const unsigned long long q = match ? mass_of(key[i], temperature, mt) : 0ull;
-    hist_add(q != 0, (key[i] >> shift) & (RADIX - 1), q, hm, hc);
   }
 }
 
@@ -172,89 +213,207 @@ struct Pick {
   unsigned long long tie_mass;  // their total mass
 };
 
-// The element (key) at which the descending running mass first exceeds
-// `target` (target < total mass). Uses the first-digit histogram hmass[0],
-// built by the caller; later passes alternate between buffers 1 and 2
-// (`flip`), so that a CTA never clears a histogram another CTA may still be
-// reading (two cluster barriers separate a read from the next clear).
-__device__ __forceinline__ Pick radix_select(unsigned long long target, const uint32_t* key, float temperature,
-                                             float mt, Shared& s, cg::cluster_group& cluster, int ncta, int& flip) {
+// Inclusive scan of the (mass, count) pairs held by threads tid < n (n a
+// multiple of 32, <= THREADS), in thread order, then the first position whose
+// running mass plus `base` exceeds `target`. Returns the position and, through
+// the references, the sums before it and the pair at it. Every thread must
+// call it.
+__device__ __forceinline__ int scan_cross(unsigned long long m, unsigned c, int n, unsigned long long base,
+                                          unsigned long long target, Shared& s, unsigned long long& excl_m,
+                                          unsigned& excl_n, unsigned long long& own_m, unsigned& own_n) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < n) {  // whole warps
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long wm = __shfl_up_sync(0xffffffffu, m, o);
+      const unsigned wc = __shfl_up_sync(0xffffffffu, c, o);
+      if (lane >= o) {
+        m += wm;
+        c += wc;
+      }
+    }
+  }
+  __syncthreads();  // warp scratch free
+  if (tid < n && lane == 31) {
+    s.warp64[warp] = m;
+    s.warp32[warp] = c;
+  }
+  __syncthreads();
+  if (tid < n) {
+    for (int w = 0; w < warp; ++w) {
+      m += s.warp64[w];
+      c += s.warp32[w];
+    }
+    s.scan_m[tid] = m;
+    s.scan_n[tid] = c;
+  }
+  // the running mass is monotonic in the position: the crossing ones are a suffix
+  const bool over = tid < n && base + m > target;
+  int first = n - __syncthreads_count(over);
+  if (first >= n) first = n - 1;  // cannot happen for target < base + total
+  excl_m = first ? s.scan_m[first - 1] : 0ull;
+  excl_n = first ? s.scan_n[first - 1] : 0u;
+  own_m = s.scan_m[first] - excl_m;
+  own_n = s.scan_n[first] - excl_n;
+  __syncthreads();  // scan arrays reused by the next scan
+  return first;
+}
+
+// Local finish: radix select over the n keys of s.merged (one value bucket),
+// in this CTA's shared memory only.
+__device__ __forceinline__ Pick local_select(int n, unsigned long long target, float temperature, float mt,
+                                             Shared& s) {
   const int tid = threadIdx.x;
   uint32_t prefix = 0, pmask = 0;
   Pick p{0, 0, 0, 0, 0};
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    int buf = 0;
-    if (pass > 0) {
-      buf = 1 + flip;
-      flip ^= 1;
-      if (tid < RADIX) {
-        s.hmass[buf][tid] = 0;
-        s.hcount[buf][tid] = 0;
-      }
-      __syncthreads();
-      accumulate(key, temperature, mt, prefix, pmask, shift, s.hmass[buf], s.hcount[buf]);
-      cluster.sync();  // every CTA's histogram complete and visible
-    }
-    // Cluster totals per digit, digit 255 first (largest keys first).
-    const int lane = tid & 31, warp = tid >> 5;
-    unsigned long long m = 0;
-    unsigned n = 0;
     if (tid < RADIX) {
-      const int d = RADIX - 1 - tid;
-      for (int r = 0; r < ncta; ++r) {
-        m += cluster.map_shared_rank(&s.hmass[buf][0], r)[d];
-        n += cluster.map_shared_rank(&s.hcount[buf][0], r)[d];
-      }
-      // inclusive scan within the warp, then across the 8 warps
+      s.pm[0][tid] = 0;
+      s.pc[0][tid] = 0;
+    }
+    __syncthreads();
+    for (int b = 0; b < n; b += THREADS) {  // uniform trip count: every lane reaches hist_add
+      const int i = b + tid;
+      const uint32_t k = i < n ? s.merged[i] : kNoKey;
+      const bool match = i < n && (k & pmask) == prefix;
+      hist_add(match, (k >> shift) & (RADIX - 1), match ? mass_of(k, temperature, mt) : 0ull, s.pm[0], s.pc[0]);
+    }
+    __syncthreads();
+    unsigned long long m = 0, em, om;
+    unsigned c = 0, en, on;
+    if (tid < RADIX) {
+      m = s.pm[0][RADIX - 1 - tid];  // largest digit first
+      c = s.pc[0][RADIX - 1 - tid];
+    }
+    const int first = scan_cross(m, c, RADIX, p.above, target, s, em, en, om, on);
+    p.above += em;
+    p.n_above += en;
+    p.ties = on;
+    p.tie_mass = om;
+    prefix |= static_cast<uint32_t>(RADIX - 1 - first) << shift;
+    pmask |= static_cast<uint32_t>(RADIX - 1) << shift;
+  }
+  p.key = prefix;
+  return p;
+}
+
+// Cluster fallback for a crossing bucket of more than CAP elements: radix
+// passes over the keys of bucket `vb`, each a cluster-wide histogram
+// (alternating buffers, so that a CTA never clears a histogram another may
+// still be reading: two cluster barriers separate a read from the next clear).
+__device__ __forceinline__ Pick cluster_select(int vb, Pick p, unsigned long long target, const uint32_t* key,
+                                               float temperature, float mt, Shared& s, cg::cluster_group& cluster,
+                                               int ncta, int& flip) {
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0, pmask = 0;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const int buf = flip;
+    flip ^= 1;
+    for (int i = tid; i < NCOPY * RADIX; i += THREADS) {
+      (&s.pm[0][0])[i] = 0;
+      (&s.pc[0][0])[i] = 0;
+    }
+    __syncthreads();
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long wm = __shfl_up_sync(0xffffffffu, m, o);
-        const unsigned wn = __shfl_up_sync(0xffffffffu, n, o);
-        if (lane >= o) {
-          m += wm;
-          n += wn;
-        }
-      }
-      if (lane == 31) {
-        s.warp64[warp] = m;
-        s.warp32[warp] = n;
-      }
+    for (int i = 0; i < EPT; ++i) {
+      const bool match = key[i] != kNoKey && (key[i] & pmask) == prefix && vbucket(key[i], temperature, mt) == vb;
+      const unsigned long long q = match ? mass_of(key[i], temperature, mt) : 0ull;
+      hist_add(q != 0, (key[i] >> shift) & (RADIX - 1), q, s.pm[(tid >> 5) % NCOPY], s.pc[(tid >> 5) % NCOPY]);
     }
     __syncthreads();
     if (tid < RADIX) {
-      for (int w = 0; w < warp; ++w) {
-        m += s.warp64[w];
-        n += s.warp32[w];
+      unsigned long long m = 0;
+      unsigned c = 0;
+#pragma unroll
+      for (int k = 0; k < NCOPY; ++k) {
+        m += s.pm[k][tid];
+        c += s.pc[k][tid];
       }
-      s.scan_m[tid] = m;
-      s.scan_n[tid] = n;
+      s.hmass[buf][tid] = m;
+      s.hcount[buf][tid] = c;
     }
-    // The running mass is monotonic in tid, so the digits that cross the
-    // target form a suffix; the first crossing one is RADIX - count.
-    const bool over = tid < RADIX && p.above + m > target;
-    int first = RADIX - __syncthreads_count(over);
-    if (first >= RADIX) first = RADIX - 1;  // cannot happen for target < mass of the prefix
-    const unsigned long long incl_m = s.scan_m[first];
-    const unsigned incl_n = s.scan_n[first];
-    const unsigned long long excl_m = first ? s.scan_m[first - 1] : 0ull;
-    const unsigned excl_n = first ? s.scan_n[first - 1] : 0u;
-    p.above += excl_m;
-    p.n_above += excl_n;
-    p.ties = incl_n - excl_n;
-    p.tie_mass = incl_m - excl_m;
+    cluster.sync();  // every CTA's histogram complete and visible
+    unsigned long long m = 0, em, om;
+    unsigned c = 0, en, on;
+    if (tid < RADIX) {
+      const int d = RADIX - 1 - tid;
+#pragma unroll
+      for (int r = 0; r < MAX_CTAS; ++r) {  // all remote loads in flight at once
+        if (r < ncta) {
+          m += cluster.map_shared_rank(&s.hmass[buf][0], r)[d];
+          c += cluster.map_shared_rank(&s.hcount[buf][0], r)[d];
+        }
+      }
+    }
+    const int first = scan_cross(m, c, RADIX, p.above, target, s, em, en, om, on);
+    p.above += em;
+    p.n_above += en;
+    p.ties = on;
+    p.tie_mass = om;
     prefix |= static_cast<uint32_t>(RADIX - 1 - first) << shift;
     pmask |= static_cast<uint32_t>(RADIX - 1) << shift;
-    __syncthreads();  // scan_m / warp scratch reused by the next pass
   }
   p.key = prefix;
+  return p;
+}
+
+// The element (key) at which the descending running mass first exceeds
+// `target` (< total mass). s.vmass / s.vcount hold the cluster's value-bucket
+// totals; `sel` (0, 1) picks this call's candidate list, so that the two
+// calls of a row never overwrite a list another CTA may still be reading.
+__device__ __forceinline__ Pick select(unsigned long long target, int sel, const uint32_t* key, float temperature,
+                                       float mt, Shared& s, cg::cluster_group& cluster, int ncta, int& flip) {
+  const int tid = threadIdx.x;
+  unsigned long long em, om;
+  unsigned en, on;
+  const int vb = scan_cross(s.vmass[tid], s.vcount[tid], VB, 0ull, target, s, em, en, om, on);
+  Pick p{0, em, en, 0, 0};
+  if (on <= static_cast<unsigned>(CAP)) {  // uniform: every CTA computed the same totals
+    // gather this CTA's keys of bucket vb, then every CTA merges all lists
+    if (tid == 0) s.cand_n[sel] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      if (key[i] != kNoKey && mass_of(key[i], temperature, mt) != 0 && vbucket(key[i], temperature, mt) == vb) {
+        const unsigned slot = atomicAdd(&s.cand_n[sel], 1u);
+        if (slot < static_cast<unsigned>(CAP)) s.cand[sel][slot] = key[i];
+      }
+    }
+    cluster.sync();
+    unsigned cnt[MAX_CTAS];
+    int total = 0;
+#pragma unroll
+    for (int r = 0; r < MAX_CTAS; ++r) {
+      cnt[r] = r < ncta ? *cluster.map_shared_rank(&s.cand_n[sel], r) : 0u;
+      if (cnt[r] > static_cast<unsigned>(CAP)) cnt[r] = CAP;
+      total += static_cast<int>(cnt[r]);
+    }
+    if (total > CAP) total = CAP;  // cannot happen: the bucket holds `on` <= CAP keys
+    for (int i = tid; i < total; i += THREADS) {
+      int r = 0, off = i;
+      while (r < MAX_CTAS - 1 && off >= static_cast<int>(cnt[r])) off -= static_cast<int>(cnt[r++]);
+      s.merged[i] = cluster.map_shared_rank(&s.cand[sel][0], r)[off];
+    }
+    __syncthreads();
+    const Pick q = local_select(total, target - p.above, temperature, mt, s);
+    p.key = q.key;
+    p.above += q.above;
+    p.n_above += q.n_above;
+    p.ties = q.ties;
+    p.tie_mass = q.tie_mass;
+  } else {
+    p = cluster_select(vb, p, target, key, temperature, mt, s, cluster, ncta, flip);
+  }
   return p;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
 top_p_kernel(const float* __restrict__ logits, int V, long long ld, float temperature, float top_p,
              const float* __restrict__ uniforms, long long* __restrict__ tokens, int* __restrict__ nucleus) {
-  __shared__ Shared s;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Shared& s = *reinterpret_cast<Shared*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int ncta = static_cast<int>(cluster.num_blocks());
@@ -299,9 +458,12 @@ top_p_kernel(const float* __restrict__ logits, int V, long long ld, float temper
   if (tid == 0) s.cta_max = best;
   cluster.sync();
   unsigned long long gbest = 0;
-  for (int r = 0; r < ncta; ++r) {
-    const unsigned long long c = *cluster.map_shared_rank(&s.cta_max, r);
-    gbest = c > gbest ? c : gbest;
+#pragma unroll
+  for (int r = 0; r < MAX_CTAS; ++r) {
+    if (r < ncta) {
+      const unsigned long long c = *cluster.map_shared_rank(&s.cta_max, r);
+      gbest = c > gbest ? c : gbest;
+    }
   }
   const float m = key_value(static_cast<uint32_t>(gbest >> 32));
   const long long argmax = static_cast<long long>(0xffffffffu - static_cast<uint32_t>(gbest & 0xffffffffu));
@@ -314,22 +476,74 @@ top_p_kernel(const float* __restrict__ logits, int V, long long ld, float temper
     return;
   }
 
-  // 2. integer masses, their total Q, and the first-digit histogram
+  // 2. integer masses, their total Q, and the value-bucket histogram
   const float mt = __fdiv_rn(m, temperature);
-  unsigned long long qsum = 0;
-#pragma unroll
-  for (int i = 0; i < EPT; ++i) qsum += mass_of(key[i], temperature, mt);
-  qsum = block_reduce<false>(qsum, s.warp64);
-  if (tid == 0) s.cta_mass = qsum;
-  if (tid < RADIX) {
-    s.hmass[0][tid] = 0;
-    s.hcount[0][tid] = 0;
+  for (int i = tid; i < VCOPY * VB; i += THREADS) {
+    (&s.vpm[0][0])[i] = 0;
+    (&s.vpc[0][0])[i] = 0;
   }
   __syncthreads();
-  accumulate(key, temperature, mt, 0u, 0u, 24, s.hmass[0], s.hcount[0]);
+  unsigned long long qsum = 0;
+  {
+    unsigned long long* vpm = s.vpm[(tid >> 5) % VCOPY];
+    unsigned* vpc = s.vpc[(tid >> 5) % VCOPY];
+    // Buckets are spread for real or random logits: plain atomics, except for
+    // a warp whose lanes all fall into one bucket (rows of equal logits),
+    // which adds once.
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const unsigned long long q = mass_of(key[i], temperature, mt);
+      qsum += q;
+      const bool has = q != 0;
+      const int b = has ? vbucket(key[i], temperature, mt) : 0;
+      const unsigned act = __ballot_sync(0xffffffffu, has);
+      if (act && warp_uniform(act, has, static_cast<uint32_t>(b))) {
+        if (has) {
+          const unsigned long long sum = group_sum(act, q);
+          if ((tid & 31) == __ffs(act) - 1) {
+            atomicAdd(&vpm[b], sum);
+            atomicAdd(&vpc[b], static_cast<unsigned>(__popc(act)));
+          }
+        }
+      } else if (has) {
+        atomicAdd(&vpm[b], q);
+        atomicAdd(&vpc[b], 1u);
+      }
+    }
+  }
+  qsum = block_reduce<false>(qsum, s.warp64);  // (its barriers also complete the histogram copies)
+  if (tid == 0) s.cta_mass = qsum;
+  {
+    unsigned long long vm = 0;
+    unsigned vc = 0;
+#pragma unroll
+    for (int k = 0; k < VCOPY; ++k) {
+      vm += s.vpm[k][tid];
+      vc += s.vpc[k][tid];
+    }
+    s.vmass[tid] = vm;
+    s.vcount[tid] = vc;
+  }
   cluster.sync();
   unsigned long long Q = 0;
-  for (int r = 0; r < ncta; ++r) Q += *cluster.map_shared_rank(&s.cta_mass, r);
+  {
+    // cluster totals per bucket, kept in registers until no CTA reads this
+    // CTA's own histogram any more (the next cluster barrier)
+    unsigned long long vm = 0;
+    unsigned vc = 0;
+#pragma unroll
+    for (int r = 0; r < MAX_CTAS; ++r) {
+      if (r < ncta) {
+        Q += *cluster.map_shared_rank(&s.cta_mass, r);
+        vm += cluster.map_shared_rank(&s.vmass[0], r)[tid];
+        vc += cluster.map_shared_rank(&s.vcount[0], r)[tid];
+      }
+    }
+    cluster.sync();
+    s.vmass[tid] = vm;
+    s.vcount[tid] = vc;
+    __syncthreads();
+  }
 
   // 3. nucleus: keep a position iff the mass before it is <= top_p * Q
   int flip = 0;
@@ -338,7 +552,7 @@ top_p_kernel(const float* __restrict__ logits, int V, long long ld, float temper
   unsigned long long kept_mass = Q;
   long long kept = V;
   if (Q > tq) {
-    const Pick p = radix_select(tq, key, temperature, mt, s, cluster, ncta, flip);
+    const Pick p = select(tq, 0, key, temperature, mt, s, cluster, ncta, flip);
     const unsigned long long q = p.ties && p.tie_mass ? p.tie_mass / p.ties : 1ull;  // ties >= 1, mass > 0
     unsigned long long k = (tq - p.above) / q + 1;
     if (k > p.ties) k = p.ties;
@@ -353,7 +567,7 @@ top_p_kernel(const float* __restrict__ logits, int V, long long ld, float temper
   unsigned long long t2 =
       static_cast<unsigned long long>(floor(static_cast<double>(u) * static_cast<double>(kept_mass)));
   if (t2 >= kept_mass) t2 = kept_mass - 1;
-  const Pick p2 = radix_select(t2, key, temperature, mt, s, cluster, ncta, flip);
+  const Pick p2 = select(t2, 1, key, temperature, mt, s, cluster, ncta, flip);
   const unsigned long long q2 = p2.ties && p2.tie_mass ? p2.tie_mass / p2.ties : 1ull;
   const unsigned j = static_cast<unsigned>((t2 - p2.above) / q2);  // which of the equal logits, in index order
 
@@ -366,7 +580,9 @@ top_p_kernel(const float* __restrict__ logits, int V, long long ld, float temper
   if (tid == 0) s.cta_ties = cta_total;
   cluster.sync();
   unsigned off = 0;
-  for (int r = 0; r < rank; ++r) off += *cluster.map_shared_rank(&s.cta_ties, r);
+#pragma unroll
+  for (int r = 0; r < MAX_CTAS; ++r)
+    if (r < rank) off += *cluster.map_shared_rank(&s.cta_ties, r);
   if (j >= off + excl && j < off + excl + mine) {
     unsigned want = j - off - excl;
 #pragma unroll
@@ -382,24 +598,35 @@ top_p_kernel(const float* __restrict__ logits, int V, long long ld, float temper
 }
 }  // namespace smp
 
-int top_p_max_vocab() { return 8 * smp::CHUNK; }
+int top_p_max_vocab() { return smp::MAX_CTAS * smp::CHUNK; }
 
 cudaError_t launch_top_p(const float* logits, int rows, int V, long long ld, float temperature, float top_p,
                          const float* uniforms, long long* tokens, int* nucleus, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const int ncta = (V + smp::CHUNK - 1) / smp::CHUNK;
-  if (V <= 0 || ncta > 8 || rows > 65535) return cudaErrorInvalidValue;
+  if (V <= 0 || ncta > smp::MAX_CTAS || rows > 65535) return cudaErrorInvalidValue;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    e = cudaFuncSetAttribute(smp::top_p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sizeof(smp::Shared)));
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(ncta);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute cl[1];
+  cl[0].id = cudaLaunchAttributeClusterDimension;
+  cl[0].val.clusterDim.x = static_cast<unsigned>(ncta);
+  cl[0].val.clusterDim.y = 1;
+  cl[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(ncta), static_cast<unsigned>(rows), 1);
   cfg.blockDim = dim3(smp::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = sizeof(smp::Shared);
   cfg.stream = stream;
-  cfg.attrs = attr;
+  cfg.attrs = cl;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, smp::top_p_kernel, logits, V, ld, temperature, top_p, uniforms, tokens, nucleus);
 }
