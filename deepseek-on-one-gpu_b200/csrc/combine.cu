@@ -33,10 +33,11 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
                                                       const uint64_t* __restrict__ peer_out, int me, int cap) {
   const int t = blockIdx.x;
   __shared__ int s_row[8];
-  __shared__ float s_w[8];
+  __shared__ __nv_bfloat162 s_w2[8];  // bf16(w[t,k]) in both halves
   if (threadIdx.x < top_k) {
     s_row[threadIdx.x] = pos[static_cast<size_t>(t) * top_k + threadIdx.x];
-    s_w[threadIdx.x] = bf16_round(w[static_cast<size_t>(t) * top_k + threadIdx.x]);
+    const __nv_bfloat16 wb = __float2bfloat16_rn(w[static_cast<size_t>(t) * top_k + threadIdx.x]);
+    s_w2[threadIdx.x] = __halves2bfloat162(wb, wb);
   }
   __syncthreads();
   const int srow = row_start[0] + t;
@@ -57,33 +58,43 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
     }
     const uint4 sv = has_shared ? __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(srow) * H) + c)
                                 : make_uint4(0, 0, 0, 0);
-    float acc[8];
+    // Packed bf16x2 arithmetic: each multiply and each add rounds its exact
+    // result to bf16 once, which is what the reference's bf16 tensor ops do
+    // (they compute in fp32, exact for a product of two bf16 values and
+    // innocuously double-rounded for a sum, then round to bf16). The _rn
+    // forms keep the compiler from fusing a multiply and the following add
+    // into one FMA, which would skip the product's rounding.
+    __nv_bfloat162 acc[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 4; ++i) acc[i] = __float2bfloat162_rn(0.f);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       if (k >= top_k || s_row[k] < 0) continue;
-      const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v[k]);
-      const float wk = s_w[k];
+      const __nv_bfloat162* vb = reinterpret_cast<const __nv_bfloat162*>(&v[k]);
+      const __nv_bfloat162 wk = s_w2[k];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = bf16_round(acc[i] + bf16_round(wk * __bfloat162float(vb[i])));
+      for (int i = 0; i < 4; ++i) acc[i] = __hadd2_rn(acc[i], __hmul2_rn(wk, vb[i]));
     }
     uint4 o;
-    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
     if (has_shared) {
-      const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(&sv);
+      // shared + bf16(routed * scale): the scale stays fp32 (a Python float
+      // in the reference), so this product is taken in fp32 and rounded
+      const __nv_bfloat162* sb = reinterpret_cast<const __nv_bfloat162*>(&sv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        ob[i] = __float2bfloat16_rn(__bfloat162float(sb[i]) + bf16_round(acc[i] * scale));
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __bfloat1622float2(acc[i]);
+        ob[i] = __hadd2_rn(sb[i], __floats2bfloat162_rn(a.x * scale, a.y * scale));
+      }
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(acc[i]);
+      for (int i = 0; i < 4; ++i) ob[i] = acc[i];
     }
     if (residual) {
       const uint4 rv = __ldg(reinterpret_cast<const uint4*>(residual + static_cast<size_t>(t) * H) + c);
-      const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+      const __nv_bfloat162* rb = reinterpret_cast<const __nv_bfloat162*>(&rv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__bfloat162float(rb[i]) + __bfloat162float(ob[i]));
+      for (int i = 0; i < 4; ++i) ob[i] = __hadd2_rn(rb[i], ob[i]);
     }
     reinterpret_cast<uint4*>(orow)[c] = o;
   }

@@ -4,7 +4,8 @@
 // [g | u] in bf16. This kernel forms
 //     h = bf16( bf16(silu(g)) * u )          (inference/ops.py:190-192: the
 //                                             reference's F.silu on bf16 and
-//                                             the bf16 product)
+//                                             the bf16 product; silu in fp32
+//                                             with the fast exp / divide)
 // and stores it in the down GEMM's activation format: one fp32 scale per row
 // and two e4m3 terms, h ~= (hi + lo) * scale. One warp per row. Rows of up to
 // 2048 features are done in one pass: every lane loads all of its g and u
@@ -17,17 +18,31 @@
 namespace dsmoe {
 
 namespace sq {
-__device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
+// silu(x) = x / (1 + e^-x) in fp32 with the fast exp and divide: a few ulp
+// of fp32 from the exactly rounded value, so bf16(silu(x)) can differ from
+// the reference's in its last bit for a small fraction of elements (the
+// kernel is bound by instruction issue; this halves its instructions).
+__device__ __forceinline__ float silu_f32(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// h = bf16(bf16(silu(g)) * u) for 8 consecutive columns.
-__device__ __forceinline__ void swiglu8(const __nv_bfloat16* g, const __nv_bfloat16* u, float* h) {
-  const uint4 gv = __ldg(reinterpret_cast<const uint4*>(g));
-  const uint4 uv = __ldg(reinterpret_cast<const uint4*>(u));
-  const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv);
-  const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uv);
+// h = bf16(bf16(silu(g)) * u) for 8 consecutive columns as 4 bf16x2 pairs:
+// the product of two bf16 values is exact in fp32, so the packed bf16
+// multiply rounds it exactly as the reference's bf16 tensor product does.
+__device__ __forceinline__ void swiglu8(const uint4& gv, const uint4& uv, __nv_bfloat162* h) {
+  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+  const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-    h[i] = bf16_round(bf16_round(silu_f32(__bfloat162float(gb[i]))) * __bfloat162float(ub[i]));
+  for (int i = 0; i < 4; ++i) {
+    const float2 g = __bfloat1622float2(g2[i]);
+    h[i] = __hmul2_rn(__floats2bfloat162_rn(silu_f32(g.x), silu_f32(g.y)), u2[i]);
+  }
+}
+
+__device__ __forceinline__ float amax8(const __nv_bfloat162* h, float amax) {
+  __nv_bfloat162 m = __habs2(h[0]);
+#pragma unroll
+  for (int i = 1; i < 4; ++i) m = __hmax2(m, __habs2(h[i]));
+  const float2 f = __bfloat1622float2(m);
+  return fmaxf(amax, fmaxf(f.x, f.y));
 }
 
 // Split 8 values (already multiplied by 448 / amax) into hi and lo e4m3 terms
@@ -104,16 +119,8 @@ __global__ void __launch_bounds__(256) swiglu_quant_1pass(const __nv_bfloat16* _
   for (int it = 0; it < NIT; ++it) {
     const int col = it * 256 + lane * 8;
     if (col < F) {
-      const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv[it]);
-      const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uv[it]);
-      float h[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        h[i] = bf16_round(bf16_round(silu_f32(__bfloat162float(gb[i]))) * __bfloat162float(ub[i]));
-        amax = fmaxf(amax, fabsf(h[i]));
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) hb[it * 4 + i] = __floats2bfloat162_rn(h[2 * i], h[2 * i + 1]);  // exact
+      swiglu8(gv[it], uv[it], hb + it * 4);
+      amax = amax8(hb + it * 4, amax);
     }
   }
 #pragma unroll
@@ -153,21 +160,25 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const __nv_bfloat16* 
   uint8_t* lo_row = hq + (static_cast<size_t>(P) + row) * F;
   float amax = 0.f;
   for (int col = lane * 8; col < F; col += 256) {
-    float h[8];
-    swiglu8(g_row + col, u_row + col, h);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(h[i]));
+    __nv_bfloat162 h[4];
+    swiglu8(__ldg(reinterpret_cast<const uint4*>(g_row + col)), __ldg(reinterpret_cast<const uint4*>(u_row + col)), h);
+    amax = amax8(h, amax);
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float inv = amax > 0.f ? 448.f / amax : 0.f;
   if (lane == 0) hs[row] = amax / 448.f;
   for (int col = lane * 8; col < F; col += 256) {
-    float h[8];
-    swiglu8(g_row + col, u_row + col, h);
+    __nv_bfloat162 h[4];
+    swiglu8(__ldg(reinterpret_cast<const uint4*>(g_row + col)), __ldg(reinterpret_cast<const uint4*>(u_row + col)), h);
+    float q[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] *= inv;
-    split_store8(h, hi_row + col, lo_row + col);
+    for (int i = 0; i < 4; ++i) {
+      const float2 v = __bfloat1622float2(h[i]);
+      q[2 * i] = v.x * inv;
+      q[2 * i + 1] = v.y * inv;
+    }
+    split_store8(q, hi_row + col, lo_row + col);
   }
 }
 }  // namespace sq
