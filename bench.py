@@ -10,12 +10,18 @@ Printed JSON keys (one line, rank 0):
   value      tokens/s over all ranks, inputs resident in HBM, CUDA-event timed
   e2e        same metric through ``moe_block`` with the input copied from pinned
              host memory and the output read back every step
-  roofline   the dominant kernel (grouped gate/up GEMM): algorithmic bytes per
-             launch / its event-timed duration, against the measured HBM peak
+  roofline   the dominant kernel (grouped gate/up GEMM): algorithmic bytes (or
+             FLOPs, whichever bound its arithmetic intensity sets) per launch /
+             its event-timed duration, against the measured peak
   cpu_baseline  the CPU oracle (a restatement of the reference's per-token
              moe_block) timed on a bounded token sample on this host
+  widened_rows  RMSNorm, the MoE layer's FFN half, the dense FFN, the expert
+             loader and next-token sampling, measured on the same GPU
 ``--impl reference`` times only that CPU path and prints its own line.
-With N > 1 every rank runs its own replica of the layer (weak scaling).
+With N > 1 (torchrun, one rank per GPU) the step is expert-parallel (config
+3: 8192 tokens per rank, each rank owning 256/N experts, token rows and
+partial sums exchanged over peer memory; ``--nccl-exchange`` for the NCCL
+all-to-all, ``--mode replica`` for independent replicas); weak scaling.
 """
 from __future__ import annotations
 
@@ -54,7 +60,7 @@ def gemm_tile(tokens: int) -> int:
 
 
 def expert_load_rates(cfg, dev, n_experts: int = 16, layer: int = 7) -> dict:
-    """Expert disk step (SURVEY's first widening row): read n R1-size experts
+    """Expert disk step (the loader that feeds the pinned expert cache): read n R1-size experts
     from a safetensors file (written just before, so from the page cache)
     into pinned host memory, with the store (packed buffers, native pread
     pool) and with the reference's own steps (safe_open, get_tensor, copy into

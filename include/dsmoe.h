@@ -201,7 +201,7 @@ DSMOE_API int dsmoe_set_gemm_sm_limit(int32_t max_ctas);
 
 /*
  * Expert parallelism over W ranks (no counterpart in the reference, which is
- * single-GPU; SURVEY's EP row). Rank d owns routed experts
+ * single-GPU). Rank d owns routed experts
  * [d * experts_per_rank, (d+1) * experts_per_rank); gate and shared expert are
  * replicated. One layer step on every rank:
  *   1. dsmoe_route on the rank's tokens.

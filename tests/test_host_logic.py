@@ -11,7 +11,9 @@ from dsmoe.config import load_config
 from dsmoe.gpu_transfer import LayerBank
 from dsmoe.synthetic import FP8_MAX, SyntheticLayer, activations, block_quantize, expert_weights, score_bias
 
-REF_ROOT = os.environ.get("DSMOE_REFERENCE_ROOT", "/root/reference")
+# the reference source tree: $DSMOE_REFERENCE_ROOT, else a "reference" folder beside this repository
+REF_ROOT = os.environ.get("DSMOE_REFERENCE_ROOT") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
 
 
 def entry(nbytes):
