@@ -57,8 +57,8 @@ def _worker(rank, world, port, q):
         q.put((rank, repr(e)))
 
 
-def test_dist_exchange_two_gloo_ranks():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_dist_exchange_gloo_ranks(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -68,4 +68,4 @@ def test_dist_exchange_two_gloo_ranks():
     results = dict(q.get(timeout=120) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
-    assert results == {0: "ok", 1: "ok"}
+    assert results == {r: "ok" for r in range(world)}
