@@ -74,7 +74,7 @@ def sample(logits: torch.Tensor, temperature: float, top_p: float,
 
 def generate_tokens(step, first_logits: torch.Tensor, max_tokens: int, eos_token_id: int | None,
                     temperature: float = 0.6, top_p: float = 0.9, generator: torch.Generator | None = None,
-                    check_every: int = 16) -> list[int]:
+                    check_every: int = 16, sampler=None) -> list[int]:
     """The decode loop of ``InferenceEngine.generate`` (``engine.py:116-151``)
     for one sequence, with the tokens kept on the device.
 
@@ -85,13 +85,15 @@ def generate_tokens(step, first_logits: torch.Tensor, max_tokens: int, eos_token
     the sequence, unkept, if it is ``eos_token_id``; at most ``max_tokens``
     tokens. The host looks at the tokens every ``check_every`` steps, so up to
     ``check_every - 1`` steps may run past the end-of-sequence token; their
-    tokens are dropped.
+    tokens are dropped. ``sampler`` (default ``sample_with_uniforms``) is the
+    per-step sampling call, with that function's arguments.
     """
     if max_tokens <= 0:
         return []
+    draw_token = sampler or sample_with_uniforms
     dev = first_logits.device
     buf = torch.empty(max_tokens, dtype=torch.int64, device=dev)
-    sample_with_uniforms(first_logits, temperature, top_p, _draw(dev, temperature, generator), out=buf[0:1])
+    draw_token(first_logits, temperature, top_p, _draw(dev, temperature, generator), out=buf[0:1])
     done = 1
     out: list[int] = []
     checked = 0
@@ -99,8 +101,8 @@ def generate_tokens(step, first_logits: torch.Tensor, max_tokens: int, eos_token
         stop = min(max_tokens, done + max(1, check_every))
         for i in range(done, stop):
             logits = step(buf[i - 1:i], i - 1)
-            sample_with_uniforms(logits[:, -1, :] if logits.dim() == 3 else logits, temperature, top_p,
-                                 _draw(dev, temperature, generator), out=buf[i:i + 1])
+            draw_token(logits[:, -1, :] if logits.dim() == 3 else logits, temperature, top_p,
+                       _draw(dev, temperature, generator), out=buf[i:i + 1])
         done = stop
         host = buf[checked:done].tolist()  # the only host read, once per chunk
         for k, t in enumerate(host):

@@ -113,3 +113,39 @@ def test_config_mirror_and_loader(tmp_path):
                                           ' "quantization_config": {"weight_block_size": [128, 128]}}')
     c2 = load_config(tmp_path, router_mode="v3")
     assert (c2.hidden_size, c2.n_routed_experts, c2.n_group, c2.router_mode) == (1024, 64, 2, "v3")
+
+
+@pytest.mark.parametrize("check_every", [1, 3, 7, 64])
+def test_generate_tokens_loop_rules(check_every):
+    """The decode loop's host rules (engine.py:116-151) with a stand-in
+    sampler (argmax on the CPU): the first token is kept even if it is the
+    end-of-sequence token, a later one ends the output unkept, at most
+    max_tokens tokens, whatever the host-check interval."""
+    from dsmoe.sampling import generate_tokens
+
+    V = 10
+    script = [3, 5, 9, 2, 9, 4, 1, 7, 8, 6, 0, 2]  # token produced by decode step i
+
+    def one_hot(t):
+        x = torch.full((1, V), -1.0)
+        x[0, t] = 1.0
+        return x
+
+    def step(token, i):  # steps past the script (run ahead of the host check) repeat it
+        return one_hot(script[i % len(script)])
+
+    def argmax_sampler(logits, temperature, top_p, u, out):
+        out.copy_(logits.argmax(dim=-1))
+        return out
+
+    def run(first, max_tokens, eos):
+        return generate_tokens(step, one_hot(first), max_tokens, eos, temperature=0.0,
+                               check_every=check_every, sampler=argmax_sampler)
+
+    assert run(4, 8, None) == [4] + script[:7]
+    assert run(4, 1, None) == [4]
+    assert run(4, 0, None) == []
+    assert run(4, 20, 9) == [4, 3, 5]            # stops at the first 9, unkept
+    assert run(9, 20, 9) == [9, 3, 5]            # the first token is kept even when it is the eos
+    assert run(4, 3, 9) == [4, 3, 5]             # max_tokens reached before the eos
+    assert run(4, 12, 0) == [4] + script[:10]    # eos at decode step 10
