@@ -388,7 +388,8 @@ cudaError_t launch_cfg(const CUtensorMap& w0, const CUtensorMap& w1, const CUten
   using C = Cfg<BN, STAGES, NBUF, NCAT>;
   static bool attr[64] = {false};
   int dev = 0;
-  cudaGetDevice(&dev);
+  const cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
     cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, NBUF, NCAT>,

@@ -149,7 +149,8 @@ cudaError_t launch_router_logits_tc(const CUtensorMap& tm_x, const CUtensorMap& 
   if (E > rtc::MAX_E || E % 16 || H % rtc::BKE) return cudaErrorInvalidValue;
   static bool attr[64] = {false};
   int dev = 0;
-  cudaGetDevice(&dev);
+  const cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
     cudaError_t e =
