@@ -96,6 +96,9 @@ def test_no_cpu_fallback():
     cfg_ = DeepSeekConfig(hidden_size=256, moe_intermediate_size=256)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.route(torch.zeros(1, 4, 256, dtype=torch.bfloat16), torch.zeros(256, 256, dtype=torch.bfloat16), cfg_)
+    from dsmoe import sample
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sample(torch.zeros(2, 100), 0.0, 0.9)
 
 
 def test_norm_and_layer_ffn_reject_bad_arguments():
