@@ -21,6 +21,12 @@ algorithm of ``sushruta/deepseek-on-one-gpu``:
     only the summation order inside the fp32 GEMM may differ (batched rows
     against a single row).
 
+The functions are device-agnostic torch code. The golden and small-shape
+checks run them on CPU tensors; the full-shape checks of the benchmark
+configurations (thousands of rows through all 257 experts) run the same code
+on CUDA tensors as a plain fp32 torch reference (TF32 off, so every matmul is
+an fp32 matmul; only its summation order differs from the CPU's).
+
 Parity is pinned: ``tests/golden/`` holds outputs of the reference's own
 ``moe_block`` and ``route`` (imported from the reference tree by
 ``tests/golden/make_golden.py``) and ``tests/test_oracle_golden.py`` checks this
@@ -114,7 +120,7 @@ def dequant(weight: torch.Tensor, scale_inv: torch.Tensor) -> torch.Tensor:
     128x128 block multiplied by that block's ``weight_scale_inv``."""
     O, I = weight.shape
     bo, bi = math.ceil(O / BLOCK), math.ceil(I / BLOCK)
-    w = torch.zeros(bo * BLOCK, bi * BLOCK, dtype=torch.float32)
+    w = torch.zeros(bo * BLOCK, bi * BLOCK, dtype=torch.float32, device=weight.device)
     w[:O, :I] = weight.float()
     w = (w.view(bo, BLOCK, bi, BLOCK) * scale_inv.float()[:, None, :, None]).view(bo * BLOCK, bi * BLOCK)
     return w[:O, :I]
@@ -180,11 +186,11 @@ def moe_block_grouped(hidden: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, 
     idx2 = idx.reshape(T, K)
     w2 = w.reshape(T, K)
     shared_out = expert_ffn(x, shared)
-    y = torch.empty(T, K, H, dtype=torch.bfloat16)
+    y = torch.empty(T, K, H, dtype=torch.bfloat16, device=x.device)
     for e in torch.unique(idx2).tolist():
         t_sel, k_sel = (idx2 == e).nonzero(as_tuple=True)
         y[t_sel, k_sel] = expert_ffn(x[t_sel], get_expert(e))
-    routed = torch.zeros(T, H, dtype=torch.bfloat16)
+    routed = torch.zeros(T, H, dtype=torch.bfloat16, device=x.device)
     for k in range(K):
         routed += (w2[:, k:k + 1].to(torch.bfloat16) * y[:, k]).to(torch.bfloat16)
     scale = routed_scaling_factor if final_scale is None else final_scale
