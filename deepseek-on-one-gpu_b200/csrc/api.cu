@@ -764,7 +764,12 @@ int dsmoe_ep_combine(const void* partials, const int32_t* tok_rows, int32_t toke
 }
 
 int dsmoe_read_status(void* workspace, int32_t* device_status, dsmoe_stream_t stream) {
-  if (!workspace || !device_status) return fail(DSMOE_ERR_INVALID, "NULL argument");
+  if (!device_status) return fail(DSMOE_ERR_INVALID, "NULL argument");
+  if (!workspace) {  // the allocation-free entry point's scratch on the current device
+    const char* err = "";
+    workspace = noalloc_status_word(&err);
+    if (!workspace) return fail(DSMOE_ERR_CUDA, "%s", err);
+  }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int v = 0;
   DSMOE_CUDA(cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));

@@ -10,6 +10,9 @@ namespace dsmoe {
 
 // Records `msg` as the calling thread's dsmoe_last_error() and returns `code`.
 int set_last_error(int code, const char* msg);
+// Device address of the current device's allocation-free scratch status word
+// (noalloc.cu); nullptr with the reason in *err on failure.
+void* noalloc_status_word(const char** err);
 
 // Group-table convention used by every kernel: group 0 is the shared expert
 // (every token, in token order), group 1 + e is routed expert e.

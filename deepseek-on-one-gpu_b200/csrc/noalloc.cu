@@ -25,8 +25,10 @@ void* g_scratch_ptr[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 
 // Device address of this device's copy of g_noalloc_scratch (set-up on the
-// first call per device). Returns nullptr and fills `err` on failure.
-void* scratch_for_current_device(std::string& err) {
+// first call per device, with that device current). Returns nullptr and
+// fills `err` on failure. `first` tells the caller that this call did the
+// set-up.
+void* scratch_for_current_device(std::string& err, bool* first = nullptr) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
@@ -34,6 +36,7 @@ void* scratch_for_current_device(std::string& err) {
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (first) *first = false;
   if (!g_scratch_ptr[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
@@ -42,11 +45,22 @@ void* scratch_for_current_device(std::string& err) {
       return nullptr;
     }
     g_scratch_ptr[dev] = p;
+    if (first) *first = true;
   }
   return g_scratch_ptr[dev];
 }
 
 }  // namespace
+
+// The status word is the first int of the scratch (the workspace layout of
+// dsmoe_expert_ffn puts it at offset 0).
+void* noalloc_status_word(const char** err) {
+  static thread_local std::string msg;
+  void* p = scratch_for_current_device(msg);
+  if (!p && err) *err = msg.c_str();
+  return p;
+}
+
 }  // namespace dsmoe
 
 extern "C" int dsmoe_expert_ffn_noalloc(const void* x, int32_t tokens, int32_t hidden, int32_t inter,
@@ -65,14 +79,20 @@ extern "C" int dsmoe_expert_ffn_noalloc(const void* x, int32_t tokens, int32_t h
     return dsmoe::set_last_error(DSMOE_ERR_WORKSPACE, buf);
   }
   std::string err;
-  void* scratch = dsmoe::scratch_for_current_device(err);
+  bool first = false;
+  void* scratch = dsmoe::scratch_for_current_device(err, &first);
   if (!scratch) return dsmoe::set_last_error(DSMOE_ERR_CUDA, err.c_str());
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // The device status word at the front must start at zero. Every other byte
-  // whose value can reach `out` is written by this call before it is read;
-  // what the previous call left behind only feeds masked padding columns.
-  cudaError_t e = cudaMemsetAsync(scratch, 0, 256, s);
-  if (e != cudaSuccess) return dsmoe::set_last_error(DSMOE_ERR_CUDA, cudaGetErrorString(e));
+  // The device status word at the front is sticky: a kernel records the first
+  // error there and only dsmoe_read_status(NULL, ...) reads and clears it, so
+  // an error is not lost to the next call. It starts at zero: the set-up
+  // clears it once (static device memory is zeroed at load as well). Every
+  // other byte whose value can reach `out` is written by a call before it is
+  // read; what an earlier call left behind only feeds masked padding columns.
+  if (first) {
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(int), s);
+    if (e != cudaSuccess) return dsmoe::set_last_error(DSMOE_ERR_CUDA, cudaGetErrorString(e));
+  }
   return dsmoe_expert_ffn(x, tokens, hidden, inter, w_gate, s_gate, w_up, s_up, w_down, s_down, out, scratch,
                           DSMOE_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -314,6 +314,9 @@ DSMOE_API int dsmoe_ipc_free(void* dev_ptr);
  *     call's contents (the call clears what must start at zero). Calls whose
  *     work can overlap on the GPU race on the array: issue them on one stream
  *     or order them with events.
+ *   - A kernel failure (a bounded wait that ran out) is recorded in the
+ *     array's error word, which stays set until dsmoe_read_status(NULL, ...)
+ *     reads and clears it; rc 0 only means the work was enqueued.
  */
 #define DSMOE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 DSMOE_API int dsmoe_expert_ffn_noalloc(const void* x, int32_t tokens, int32_t hidden, int32_t inter,
@@ -346,7 +349,11 @@ DSMOE_API int dsmoe_sample_top_p(const float* logits, int32_t rows, int32_t voca
                                  float temperature, float top_p, const float* uniforms, int64_t* tokens,
                                  int32_t* nucleus_sizes, dsmoe_stream_t stream);
 
-/* Reads (synchronously) and clears the device error word kept in `workspace`. */
+/* Reads (synchronously) and clears the device error word kept in `workspace`.
+ * workspace == NULL reads the error word of dsmoe_expert_ffn_noalloc's
+ * library-owned scratch on the current device: that entry point has no
+ * workspace argument, and its error word stays set (first error wins) until
+ * read here, so a failure is not lost to the next call. */
 DSMOE_API int dsmoe_read_status(void* workspace, int32_t* device_status, dsmoe_stream_t stream);
 
 #ifdef __cplusplus
