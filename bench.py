@@ -17,6 +17,13 @@ Printed JSON keys (one line, rank 0):
              moe_block) timed on a bounded token sample on this host
   widened_rows  RMSNorm, the MoE layer's FFN half, the dense FFN, the expert
              loader and next-token sampling, measured on the same GPU
+  decode_rows   the same layer at decode batches T=8 and T=64 (tokens/s and
+             the GEMMs' fraction of measured HBM bandwidth)
+  streaming_config5  32 steps of config 5 (B=1 decode through 8 layers,
+             experts in pinned host memory): tokens/s, host-link GB/s, slot
+             hit rate
+  stages_ms  per-kernel CUDA-event times, recorded by the library at its
+             stage boundaries inside the timed steps
 ``--impl reference`` times only that CPU path and prints its own line.
 With N > 1 (torchrun, one rank per GPU) the step is expert-parallel (config
 3: 8192 tokens per rank, each rank owning 256/N experts, token rows and
@@ -47,16 +54,12 @@ UNIT = "tokens/s"
 H, F, E, TOPK = 7168, 2048, 256, 8
 LAYER = 3
 FP8_DENSE_NOMINAL_TFLOPS = 4500.0
-# DRAM bytes (read + write) per gate/up work unit (one 128-row weight tile x
-# one token tile) measured by ncu on a 33-expert, T=512 launch of the same
-# kernel: 1.109 GB over 1,152 units. The full-size launch is too large for a
-# multi-pass ncu capture, so its traffic is this figure times its units.
-GATEUP_DRAM_BYTES_PER_UNIT = 1.0947e9 / 1152  # ncu DRAM bytes of the 33-expert T=512 gate/up capture per work unit
-
-
-def gemm_tile(tokens: int) -> int:
-    """Token tile the library picks for a launch over `tokens` tokens."""
-    return 32 if tokens <= 32 else 64 if tokens <= 64 else 128 if tokens <= 128 else 160
+# DRAM bytes (read + write) per launch of a grouped GEMM, measured by ncu on
+# exactly the workload bench.py runs (one-pass capture of
+# dram__bytes_read.sum + dram__bytes_write.sum; the profile summaries under
+# profiles/ give the command). Keyed (stage, config, tokens per GPU, routed
+# experts); a workload without a capture reports traffic null.
+MEASURED_DRAM_BYTES: dict[tuple[str, int, int, int], float] = {}
 
 
 def expert_load_rates(cfg, dev, n_experts: int = 16, layer: int = 7) -> dict:
@@ -192,68 +195,101 @@ class ClockSampler:
                 "samples_in_timed_region": len(inside)}
 
 
-def cpu_sample(x_cpu, gate_cpu, get_expert, shared, budget_s: float, max_tokens: int):
-    """Time the oracle's per-token restatement of the reference's moe_block on
-    as many tokens as fit in ~budget_s (at least one)."""
+def workload_config(args, world: int) -> dict:
+    """The ``config`` object of the bench line, shared by both arms so that
+    the reference arm reports exactly the workload of this arm."""
+    ep = world > 1 and args.mode == "ep"
+    T, E_ = args.tokens, args.experts
+    if ep:
+        workload = (f"1 DeepSeek-R1 MoE layer, expert-parallel over {world} GPUs ({E_ // world} experts per GPU, "
+                    f"gate and shared expert replicated), T={T} tokens per GPU, "
+                    f"{'NCCL all-to-all' if args.nccl_exchange else 'peer-memory'} dispatch/combine "
+                    f"(config {args.config})")
+    else:
+        workload = (f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, {E_}+1 experts resident "
+                    f"(config {args.config})" + ("; independent replica per GPU" if world > 1 else ""))
+    c = {"workload": workload, "tokens_per_gpu": T, "hidden": H, "moe_intermediate": F, "experts": E_,
+         "top_k": TOPK, "router": "v3" if args.config == 4 else "ref", "baseline_config": args.config,
+         "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
+         "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU"}
+    if ep:
+        c.update({"ep_exchange": "NCCL all-to-all" if args.nccl_exchange else "peer memory (IPC-mapped buffers)",
+                  "ep_overlap": not args.no_overlap, "ep_chunks": args.chunks, "ep_sm_reserve": args.sm_reserve})
+    return c
+
+
+def time_cpu_reference(x_sample, gate, get_expert, shared, steps: int, warmup: int, bias=None):
+    """The reference's per-token ``moe_block`` (restated step by step by the
+    oracle, ``inference/forward.py:112-153``) on the host cores: every step
+    runs the same token sample through it. The experts the sample routes to
+    are fetched before the timed region (the reference's weight store holds
+    them in its pinned host cache). Returns (tokens/s, seconds timed)."""
     from oracle import moe_oracle as O
 
     torch.set_num_threads(os.cpu_count() or 1)
-    O.moe_block_literal(x_cpu[:1].view(1, 1, -1), gate_cpu, get_expert, shared)  # warm (dequant, threads)
-    done, t0 = 0, time.perf_counter()
-    while done < max_tokens:
-        O.moe_block_literal(x_cpu[done:done + 1].view(1, 1, -1), gate_cpu, get_expert, shared)
-        done += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
+    n = x_sample.shape[0]
+    if bias is None:
+        route_fn, scale = None, 2.5
+        idx, _ = O.route_ref(x_sample, gate)
+    else:
+        def route_fn(h):
+            return O.route_v3(h, gate, bias)
+        scale = 1.0  # the bias-corrected router's weights carry the factor
+        idx, _ = O.route_v3(x_sample, gate, bias)
+    experts = {e: get_expert(e) for e in sorted(set(idx.reshape(-1).tolist()))}
+    xs = x_sample.view(1, n, -1)
+    for _ in range(warmup):
+        O.moe_block_literal(xs, gate, experts.__getitem__, shared, route_fn=route_fn, routed_scaling_factor=scale)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        O.moe_block_literal(xs, gate, experts.__getitem__, shared, route_fn=route_fn, routed_scaling_factor=scale)
     dt = time.perf_counter() - t0
-    return done / dt, done, dt
+    return n * steps / dt, dt
 
 
-def run_reference(args, rank):
+def run_reference(args, rank, world):
+    """``--impl reference``: the reference's CPU path on this host's cores, on
+    this arm's workload. Each step is a bounded sample of it: the first
+    ``--ref-tokens-per-step`` tokens of rank 0's batch through the per-token
+    loop; the loop's cost is linear in the token count, so tokens/s
+    extrapolates to the whole batch."""
     if rank != 0:
         return
     from dsmoe.synthetic import SyntheticLayer, activations
 
-    T = args.tokens
-    L = SyntheticLayer(1, LAYER, H, F, E, "cpu", cache=True)
-    x = activations(1, T, H)
-    torch.set_num_threads(os.cpu_count() or 1)
-    from oracle import moe_oracle as O
-
-    sample = x[: args.ref_tokens_per_step].view(1, -1, H)
-    for _ in range(args.warmup):
-        O.moe_block_literal(sample, L.gate, L.expert, L.shared())
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        O.moe_block_literal(sample, L.gate, L.expert, L.shared())
-    dt = time.perf_counter() - t0
-    n = args.steps * sample.shape[1]
-    v = n / dt
+    T, n = args.tokens, args.ref_tokens_per_step
+    seed = {2: 1, 3: 2, 4: 3}.get(args.config, 1)
+    ep = world > 1 and args.mode == "ep"
+    L = SyntheticLayer(seed, LAYER, H, F, args.experts, "cpu", bias_zipf=1.1 if args.config == 4 else None,
+                       cache=True)
+    x = activations(1000 * seed if ep else seed, n, H)  # rank 0's first n tokens (same generator, CPU stream)
+    v, dt = time_cpu_reference(x, L.gate, L.expert, L.shared(), args.steps, args.warmup,
+                               bias=L.bias if args.config == 4 else None)
+    sample = (f"{n} tokens of rank 0's T={T} batch per step through the oracle's step-by-step restatement of the "
+              f"reference moe_block (inference/forward.py:112-153; the reference tree does not travel to this "
+              f"host), {args.steps} steps in {dt:.1f} s; experts of the same seeds and distributions generated "
+              f"on the CPU; tokens/s is linear in T")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
-        "config": {"workload": f"1 MoE layer, prefill T={T} (config 2 shape), per-token reference loop",
-                   "tokens_per_step_sample": sample.shape[1], "extrapolated": True},
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"{n} tokens of the T={T} batch through the oracle's per-token restatement of "
-                                   f"moe_block (inference/forward.py:112-153); tokens/s is linear in T"},
+                         "sample": sample},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_streaming(args, rank, world, local):
+def streaming_measure(local: int, steps: int, warmup: int, prefetch: bool = True) -> dict:
     """Config 5: B=1 decode steps through 8 MoE layers (seeds 10..17), all
     routed experts in pinned host memory, a 64-expert GPU slot cache per layer
-    (+ the shared expert), next-layer prefetch on a side stream."""
+    (+ the shared expert), next-layer prefetch on a side stream. Returns the
+    measured figures (device-timed)."""
     from dsmoe import DeepSeekConfig, SyntheticWeightStore
     from dsmoe.streaming import StreamingDecoder
     from dsmoe.synthetic import activations
 
-    if rank != 0:
-        return
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     layers = list(range(8))
     cfg = DeepSeekConfig()
@@ -276,16 +312,15 @@ def run_streaming(args, rank, world, local):
     torch.cuda.synchronize()
     link_gbs = 3 * src.nbytes / (c0.elapsed_time(c1) / 1e3) / 1e9
     del src, dst
-    dec = StreamingDecoder(cfg, store, dev, layers, slots_per_layer=65, prefetch=not args.no_prefetch)
+    dec = StreamingDecoder(cfg, store, dev, layers, slots_per_layer=65, prefetch=prefetch)
     # a new token every step (N(0,1) hidden state), carried through the 8 layers
-    h_host = activations(10, args.warmup + args.steps, H).pin_memory()
+    h_host = activations(10, warmup + steps, H).pin_memory()
     out_host = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
-    for i in range(args.warmup):
+    for i in range(warmup):
         dec.step(h_host[i:i + 1].to(dev))
     torch.cuda.synchronize()
     b0, m0, hit0 = dec.gt.bytes_h2d, dec.gt.slot_misses, dec.gt.slot_hits
     p0, u0 = dec.predicted, dec.predicted_used
-    steps = args.steps
     sampler = ClockSampler({local})
     sampler.start()
     time.sleep(0.3)
@@ -293,7 +328,7 @@ def run_streaming(args, rank, world, local):
     t_begin = time.time()
     e0.record()
     for i in range(steps):
-        hd = h_host[args.warmup + i: args.warmup + i + 1].to(dev, non_blocking=True)  # the token in
+        hd = h_host[warmup + i: warmup + i + 1].to(dev, non_blocking=True)  # the token in
         h = dec.step(hd)
         out_host.copy_(h, non_blocking=True)  # its final hidden state out
     e1.record()
@@ -303,25 +338,41 @@ def run_streaming(args, rank, world, local):
     moved = dec.gt.bytes_h2d - b0
     misses, hits = dec.gt.slot_misses - m0, dec.gt.slot_hits - hit0
     achieved = moved / (steps * ms / 1e3) / 1e9
+    out = {"tokens_per_s": 1e3 / ms, "ms_per_step": ms, "steps": steps, "warmup": warmup,
+           "host_link_GB_s": achieved, "pinned_copy_GB_s": link_gbs, "host_link_frac": achieved / link_gbs,
+           "h2d_gb_per_step": moved / steps / 1e9, "slot_hit_rate": hits / max(1, hits + misses),
+           "misses_per_layer_step": misses / (steps * len(layers)),
+           "prefetch_precision": (dec.predicted_used - u0) / max(1, dec.predicted - p0),
+           "prefetched_experts": dec.gt.prefetched, "pinned_host_gb": pinned / 1e9, "host_setup_s": setup_s,
+           "layers": len(layers), "clocks": clocks}
+    del dec, store
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_streaming(args, rank, world, local):
+    """Config 5 as its own bench line (``--config 5``)."""
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    r = streaming_measure(local, args.steps, args.warmup, prefetch=not args.no_prefetch)
     line = {
-        "metric": METRIC, "value": 1e3 / ms, "unit": UNIT, "n_gpus": 1, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
+        "metric": METRIC, "value": r["tokens_per_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
         "data": "synthetic (seeded; per-layer seeds 10..17)",
         "config": {"workload": "B=1 decode through 8 DeepSeek-R1 MoE layers, experts in pinned host memory "
                                "(config 5), h <- h + moe(h) per layer",
-                   "slots_per_layer": 64, "prefetch": not args.no_prefetch, "pinned_host_gb": pinned / 1e9,
-                   "host_setup_s": setup_s, "baseline_config": 5},
-        "e2e": {"value": 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
-        "roofline": {"kernel": "expert H2D copies (host link)", "bound": "host-link", "achieved": achieved,
-                     "peak": link_gbs, "unit": "GB/s", "frac": achieved / link_gbs,
+                   "slots_per_layer": 64, "prefetch": not args.no_prefetch, "pinned_host_gb": r["pinned_host_gb"],
+                   "host_setup_s": r["host_setup_s"], "baseline_config": 5},
+        "e2e": {"value": r["tokens_per_s"], "unit": UNIT, "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
+        "roofline": {"kernel": "expert H2D copies (host link)", "bound": "host-link", "achieved": r["host_link_GB_s"],
+                     "peak": r["pinned_copy_GB_s"], "unit": "GB/s", "frac": r["host_link_frac"],
                      "peak_source": "measured pinned->device copy of 1 GiB in this run", "traffic": None},
-        "streaming": {"h2d_gb_per_step": moved / steps / 1e9, "slot_hit_rate": hits / max(1, hits + misses),
-                      "misses_per_layer_step": misses / (steps * len(layers)),
-                      "prefetch_precision": (dec.predicted_used - u0) / max(1, dec.predicted - p0),
-                      "prefetched_experts": dec.gt.prefetched},
-        "gpu_launches": 9 * len(layers) * steps,
-        "clocks": clocks,
+        "streaming": {k: r[k] for k in ("h2d_gb_per_step", "slot_hit_rate", "misses_per_layer_step",
+                                        "prefetch_precision", "prefetched_experts")},
+        "gpu_launches": 9 * r["layers"] * args.steps,
+        "clocks": r["clocks"],
         "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)
@@ -351,11 +402,14 @@ def main():
                     help="expert-parallel step: NCCL all-to-all instead of the default peer-memory exchange")
     ap.add_argument("--no-overlap", action="store_true",
                     help="expert-parallel step: exchange and GEMMs in one stream, one after the other")
-    ap.add_argument("--cpu-budget-s", type=float, default=15.0)
-    ap.add_argument("--ref-tokens-per-step", type=int, default=2)
+    ap.add_argument("--ref-tokens-per-step", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--experts", type=int, default=E, help="routed experts (32 per group); smaller = profiling case")
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the T=8 / T=64 decode rows of the N=1 line")
+    ap.add_argument("--no-streaming", action="store_true",
+                    help="skip the config-5 streaming row of the N=1 line (90 GB of pinned host memory)")
+    ap.add_argument("--no-widened", action="store_true", help="skip the widened rows of the N=1 line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -368,7 +422,7 @@ def main():
     if args.tokens is None:
         args.tokens = {2: 4096, 3: 8192, 4: 16384, 5: 1}[args.config]
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
 
     if args.config == 5:
@@ -423,6 +477,17 @@ def main():
             return moe_block(inp, LAYER, store, gt, cfg)
 
     # ---------------------------------------------------------- device-timed
+    # Single-GPU step: the library records one set of stage-boundary events
+    # per timed step (dsmoe_set_profile_events; on the launching stream), so
+    # the per-kernel times and the roofline come from the timed steps
+    # themselves. The expert-parallel step is timed whole; its phases are
+    # measured in a separate pass below.
+    names = ["router", "permute", "gate_up", "swiglu_quant", "down", "combine"]
+    evsets = None if ep else [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+                              for _ in range(args.steps)]
+    for evs in evsets or []:
+        for e in evs:
+            e.record()  # create the CUDA events before the timed region
     for _ in range(args.warmup):
         step(x)
     torch.cuda.synchronize()
@@ -436,11 +501,15 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_begin = time.time()
     e0.record()
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        if evsets:
+            set_profile_events(evsets[i])
         step(x)
     e1.record()
     torch.cuda.synchronize()
     t_end = time.time()
+    if evsets:
+        set_profile_events(None)
     if world > 1:
         dist.barrier()
     clocks = sampler.stop((t_begin, t_end)) if rank == 0 else None
@@ -452,31 +521,29 @@ def main():
     value = world * T / (ms_max / 1000.0)
 
     # ------------------------------------------------- per-stage (roofline)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
-    set_profile_events(evs)
-    names = ["router", "permute", "gate_up", "swiglu_quant", "down", "combine"]
-    if ep:
-        names[1] = "dispatch+all_to_all+permute"
     stage_ms = [0.0] * len(names)
-    n_prof = min(20, max(3, args.steps // 2))
-    for _ in range(n_prof):
-        if ep:
-            # stage events come from the route and the rank's expert GEMMs; the
-            # shared-expert FFN in the last phase must not re-record them
+    if evsets:
+        for evs in evsets:
+            for i in range(len(names)):
+                stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / len(evsets)
+        out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)  # the (deterministic) routing
+    else:
+        # the rank's expert GEMMs phase by phase (events recorded by the
+        # library at its stage boundaries), after the timed region
+        names[1] = "dispatch+all_to_all+permute"
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        n_prof = min(20, max(3, args.steps // 2))
+        for _ in range(n_prof):
+            set_profile_events(evs)
             counts_d, tok_rows, send_x, meta = ep_layer.dispatch(x)
             sc, rc = ep_layer.exchange.counts(counts_d)
             recv_meta = ep_layer.exchange.rows(meta, sc, rc)
             part = ep_layer.compute(ep_layer.exchange.rows(send_x, sc, rc), recv_meta)
-            set_profile_events(None)
+            set_profile_events(None)  # the shared-expert FFN must not re-record them
             ep_layer.finish(x, ep_layer.exchange.rows(part, rc, sc), tok_rows)
             torch.cuda.synchronize()
-            set_profile_events(evs)
-        else:
-            out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)
-        torch.cuda.synchronize()
-        for i in range(len(names)):
-            stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
-    set_profile_events(None)
+            for i in range(len(names)):
+                stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
     ep_phases = None
     if ep:
         # the one-chunk step phase by phase, events on the compute stream
@@ -541,10 +608,7 @@ def main():
     dominant = "gate_up" if gu_ms >= dn_ms else "down"
     dom_bytes, dom_ms = (gateup_bytes, gu_ms) if dominant == "gate_up" else (down_bytes, dn_ms)
     dom_flops = 2.0 * rows * (2 * F if dominant == "gate_up" else F) * H  # algorithmic (one pass over x)
-    tile = gemm_tile(rows if ep else T)
-    per_group = ([] if ep else [T]) + counts.tolist()
-    gateup_units = sum((2 * F // 128) * ((c + tile - 1) // tile) for c in per_group)
-    traffic = GATEUP_DRAM_BYTES_PER_UNIT * gateup_units if dominant == "gate_up" else None
+    traffic = None if ep else MEASURED_DRAM_BYTES.get((dominant, args.config, T, cfg.n_routed_experts))
     # The bound is the roof the launch's algorithmic intensity meets first:
     # FP8 tensor peak taken as twice the measured bf16 GEMM rate (sustained:
     # the kernel is timed inside a step).
@@ -561,8 +625,11 @@ def main():
                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "peak_source": peak_src,
                     "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
                     "algorithmic_flops_per_launch": dom_flops}
-    roofline["traffic_source"] = ("ncu DRAM bytes per work unit of a 33-expert T=512 capture x units of this "
-                                  "launch" if traffic else None)
+    roofline["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch on this "
+                                  "workload (profiles/)" if traffic else None)
+    roofline["timing"] = ("mean of the launch's CUDA-event duration over the timed steps (events recorded by the "
+                          "library at its stage boundaries on the launching stream)" if not ep else
+                          "separate profiling pass after the timed region")
     layer_bytes = gateup_bytes + swiglu_bytes + down_bytes
     layer_ms = sum(stage_ms)
 
@@ -626,7 +693,7 @@ def main():
     # RMSNorm alone, and the dense FFN of layers 0-2 (intermediate 18432)
     # through the same FP8 GEMM, on this batch. Device-timed.
     widened = None
-    if world == 1 and not ep:
+    if world == 1 and not ep and not args.no_widened:
         from dsmoe import dense_ffn, moe_layer_ffn, rms_norm
         from dsmoe.synthetic import expert_weights
 
@@ -654,6 +721,58 @@ def main():
                    "dense_ffn_ms": dn_ms, "dense_ffn_tflops": 2.0 * T * 3 * 18432 * H / (dn_ms / 1e3) / 1e12,
                    "dense_ffn_weight_GB": dense_bytes / 1e9, **loader, **sampler}
         del dense_w
+    # -------------------------------- decode batches (north star: T=64) --
+    # The same layer and bank at decode batch sizes, timed like the main
+    # step (CUDA events per stage, inside the timed steps).
+    decode = None
+    if world == 1 and not ep and args.config == 2 and not args.no_decode:
+        decode = {}
+        for Td in (8, 64):
+            xd = activations(seed + 100 + Td, Td, H, device=dev)
+            n_d = 50
+            ev_d = [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)] for _ in range(n_d)]
+            for evs in ev_d:
+                for e in evs:
+                    e.record()
+            for _ in range(5):
+                step(xd)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for i in range(n_d):
+                set_profile_events(ev_d[i])
+                step(xd)
+            b.record()
+            torch.cuda.synchronize()
+            set_profile_events(None)
+            ms_d = a.elapsed_time(b) / n_d
+            st = [sum(evs[i].elapsed_time(evs[i + 1]) for evs in ev_d) / n_d for i in range(len(names))]
+            _, idx_d, _ = moe_block(xd, LAYER, store, gt, cfg, return_routing=True)
+            touched_d = int(torch.unique(idx_d).numel()) + 1  # + the shared expert
+            rows_d = Td * TOPK + Td
+            gu_b = touched_d * w13 + rows_d * (H * 2 + (H // 128) * 4) + rows_d * 2 * F * 2
+            dn_b = touched_d * w2 + rows_d * (F * 2 + (F // 128) * 4) + rows_d * H * 2
+            decode[f"t{Td}"] = {
+                "tokens_per_s": Td / (ms_d / 1e3), "ms_per_step": ms_d, "steps": n_d,
+                "experts_touched": touched_d, "stages_ms": dict(zip(names, st)),
+                "gate_up_hbm_frac": gu_b / (st[2] / 1e3) / 1e9 / hbm_peak,
+                "down_hbm_frac": dn_b / (st[4] / 1e3) / 1e9 / hbm_peak,
+                "step_hbm_frac": (gu_b + dn_b) / (ms_d / 1e3) / 1e9 / hbm_peak,
+                "algorithmic_bytes_gemms": gu_b + dn_b}
+        decode["note"] = ("hbm fractions: algorithmic bytes (weights of the experts touched + activation rows in "
+                          "and out) / CUDA-event time, of measured HBM " + f"{hbm_peak:.0f} GB/s")
+
+    # ------------------------------------- config 5 (streaming decode) ----
+    streaming = None
+    if world == 1 and not ep and args.config == 2 and not args.no_streaming:
+        try:
+            import psutil
+            enough = psutil.virtual_memory().available > 120e9
+        except Exception:
+            enough = False
+        streaming = (streaming_measure(local, 32, 3) if enough else
+                     {"skipped": "less than 120 GB of free host memory for the 90 GB pinned expert store"})
+
     status = Workspace.get(dev).status()
 
     # ---------------------------------------------------------- CPU oracle
@@ -662,18 +781,15 @@ def main():
         def get_expert(e):
             return {p: (w.cpu(), s.cpu()) for p, (w, s) in bank.views(e + 1).items()}
 
-        cache = {}
-
-        def cached(e):
-            if e not in cache:
-                cache[e] = get_expert(e)
-            return cache[e]
-
         shared = {p: (w.cpu(), s.cpu()) for p, (w, s) in bank.views(0).items()}
-        v, n, dt = cpu_sample(x.cpu(), store.get_gate_weight(LAYER).cpu(), cached, shared, args.cpu_budget_s, 64)
+        n_cpu = args.ref_tokens_per_step
+        v, dt = time_cpu_reference(x[:n_cpu].cpu(), store.get_gate_weight(LAYER).cpu(), get_expert, shared,
+                                   steps=2, warmup=1, bias=store.get_gate_bias(LAYER).cpu() if skew else None)
         cpu = {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"{n} tokens of the T={T} batch through the oracle's per-token restatement of the "
-                         f"reference moe_block in {dt:.1f} s; tokens/s extrapolates linearly in T"}
+               "sample": f"the first {n_cpu} tokens of the T={T} batch, 2 timed passes ({dt:.1f} s) through the "
+                         f"oracle's step-by-step restatement of the reference moe_block "
+                         f"(inference/forward.py:112-153), experts copied from this run's bank beforehand; "
+                         f"tokens/s extrapolates linearly in T (the reference loops per token)"}
 
     if rank == 0:
         line = {
@@ -681,29 +797,15 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) FP8 block-quantised experts)",
-            "config": {"workload": (f"1 DeepSeek-R1 MoE layer, expert-parallel over {world} GPUs "
-                                    f"({cfg.n_routed_experts // world} experts per GPU, gate and shared expert "
-                                    f"replicated), T={T} tokens per GPU, "
-                                    f"{'NCCL all-to-all' if args.nccl_exchange else 'peer-memory'} dispatch/combine "
-                                    f"(config {args.config})")
-                                   if ep else
-                                   (f"1 DeepSeek-R1 MoE layer, prefill T={T} tokens per GPU, "
-                                    f"{cfg.n_routed_experts}+1 experts resident (config {args.config})"
-                                    + ("; independent replica per GPU" if world > 1 else "")),
-                       "tokens_per_gpu": T, "hidden": H, "moe_intermediate": F, "experts": cfg.n_routed_experts, "top_k": TOPK,
-                       "router": cfg.router_mode, "baseline_config": args.config,
-                       "hottest_expert_over_mean": hottest_over_mean,
-                       "l2": "weights 11.3 GB per step > 126 MB L2 (no flush needed)",
-                       "parallelism": (f"ep{world}" if ep else f"replica x{world}") if world > 1 else "single GPU",
-                       **({"ep_exchange": "NCCL all-to-all" if args.nccl_exchange else "peer memory (IPC-mapped buffers)",
-                            "ep_overlap": not args.no_overlap, "ep_chunks": args.chunks,
-                            "ep_sm_reserve": args.sm_reserve} if ep else {})},
+            "config": workload_config(args, world),
+            "routing": {"hottest_expert_over_mean": hottest_over_mean},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2,
                     "copies": "pinned host buffers; H2D and D2H on their own streams, double-buffered, "
                               "overlapping the neighbouring steps' compute"},
             "roofline": roofline,
             "stages_ms": dict(zip(names, stage_ms)),
+            "stages_sum_over_step": sum(stage_ms) / ms_max,
             **({"ep_phases_ms": ep_phases} if ep_phases else {}),
             "layer": {"algorithmic_bytes": layer_bytes, "GB_s": layer_bytes / (layer_ms / 1e3) / 1e9,
                       "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm_peak,
@@ -711,6 +813,8 @@ def main():
                       "fp8_frac_of_nominal_dense": algo_flops / (ms_max / 1e3) / 1e12 / FP8_DENSE_NOMINAL_TFLOPS,
                       "experts_touched": touched},
             **({"widened_rows": widened} if widened else {}),
+            **({"decode_rows": decode} if decode else {}),
+            **({"streaming_config5": streaming} if streaming else {}),
             # library kernels per step: router 2, count/plan/scatter 3, GEMMs 2, swiglu 1, combine 1;
             # expert-parallel: + dispatch 3, + shared-expert FFN 5 (its own plan/scatter/GEMMs/swiglu)
             "gpu_launches": (18 if ep else 9) * args.steps,
