@@ -24,24 +24,31 @@
 // tiles 0..F/128-1 read the gate bank, the rest the up bank) and the output
 // row is [g | u] (2F wide); swiglu_quant.cu forms h = silu(g) * u.
 //
-// Warp roles (608 threads, one CTA per SM, persistent over work units):
-//   warp 0      TMA producer (one thread)
+// Warp roles (one CTA per SM, persistent over work units):
+//   warp 0      TMA producer (one thread); also prefetches the weight tiles
+//               PF_DIST K steps ahead into L2, across unit boundaries
 //   warp 1      TMEM allocator + MMA issuer for even K steps (one thread)
-//   warps 2-17  epilogue: warp w reads TMEM lane quadrant (w % 4) and the
-//               column group ((w - 2) / 4) of BN / 4 accumulator columns.
-//   warp 18     MMA issuer for odd K steps (one thread)
+//   warp 2      MMA issuer for odd K steps (one thread)
+//   warp 3      unit planner: decodes the CTA's work units ahead of time into
+//               a shared-memory ring (rows, weight row, MMA width and the
+//               unit's first 32 weight scales), so that no other role waits on
+//               a chain of dependent global loads at a unit boundary
+//   warps 4..   epilogue, EPI_WARPS of them: warp w reads TMEM lane quadrant
+//               (w % 4) and one column group of BN / (EPI_WARPS / 4) (<= 32)
+//               columns, in TMEM loads of up to 16 columns per term.
 // Two issuers: a thread that waits on an mbarrier between its MMA batches
 // leaves the tensor pipe idle for a few hundred cycles each time; with the
 // K steps split by parity one issuer's MMAs run while the other waits. Every
 // K step writes its own TMEM buffer and smem stage, so the two streams are
 // independent; each issuer commits only its own MMAs.
-// The SM's register file is split over four 16K-register sub-partitions and
-// 19 warps put 5 warps on some of them, so the kernel is capped at 96
-// registers per thread.
+// At a unit boundary the epilogue warps store the finished tile and start the
+// next one from values already in shared memory; the MMA meanwhile runs up to
+// NBUF - 1 K steps of the next unit ahead.
 // Activation tiles are one TMA box of BN rows per term (hi, lo); groups of at
 // most 64 tokens use 32-row boxes instead so decode steps do not pull BN rows.
 // Work unit = (group, 128-feature tile, BN-token tile); units are ordered
-// group-major, then feature tile, then token tile.
+// group-major, then feature tile, then token tile; CTA b takes units b,
+// b + gridDim.x, ...
 #include "common.cuh"
 #include "kernels.h"
 
@@ -51,13 +58,28 @@ namespace gg {
 constexpr int BM = 128;   // weight rows (output features) per tile
 constexpr int BK = 128;   // K bytes per stage
 constexpr int SUB = 32;   // token rows per small activation TMA box
-constexpr int NUM_EPI_WARPS = 16;
-constexpr int NUM_MMA_ISSUERS = 2;
-constexpr int NUM_THREADS = (2 + NUM_EPI_WARPS + 1) * 32;
-constexpr int ISSUER_B_WARP = 2 + NUM_EPI_WARPS;
 constexpr int MAX_GROUPS = 264;
+constexpr int RING = 4;       // unit-plan entries in flight
+constexpr int SW_WIN = 32;    // weight scales per window (one per lane)
+constexpr int PF_DIST = 8;    // K steps of L2 prefetch ahead of the TMA loads
+constexpr int PLAN_WARP = 3;
+constexpr int EPI_WARP0 = 4;
 
-template <int BN_, int STAGES_, int NBUF_, bool NCAT_>
+// One work unit as the planner hands it to the other roles.
+struct UnitPlan {
+  int32_t ncols;    // valid token columns of the tile
+  int32_t row0;     // first activation / output row of the tile
+  int32_t wrow;     // first weight row in the bank map (slot * M + feature tile * 128)
+  int32_t mat;      // weight matrix (0 or 1)
+  int32_t mrow;     // first output feature inside the matrix
+  int32_t nmma;     // MMA N (columns written to TMEM per K step)
+  int32_t wsc_off;  // offset of the tile's weight-scale row ([K/128] floats)
+  int32_t pad;
+  float sw[SW_WIN]; // weight scales of K blocks 0..31
+};
+static_assert(sizeof(UnitPlan) == 160, "plan entry size");
+
+template <int BN_, int STAGES_, int NBUF_, bool NCAT_, int EPI_WARPS_>
 struct Cfg {
   static constexpr int BN = BN_;                  // max tokens per tile
   static constexpr int STAGES = STAGES_;
@@ -66,51 +88,67 @@ struct Cfg {
   // tokens one MMA covers both (N = 2 * BN, columns [0,BN) hi, [BN,2BN) lo),
   // halving the MMA count; wider tiles accumulate hi then lo along K.
   static constexpr bool NCAT = NCAT_;
+  static constexpr int EPI_WARPS = EPI_WARPS_;
+  static constexpr int NUM_CG = EPI_WARPS / 4;    // column groups
+  static constexpr int NUM_THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
   static constexpr int TCOLS = NCAT ? 2 * BN : BN;  // TMEM columns per buffer
-  static constexpr int EPI_COLS = BN / 4;         // accumulator columns per epilogue warp
-  static constexpr int CHUNK = EPI_COLS % 16 ? 8 : 16;  // columns per TMEM load
+  static constexpr int EPI_COLS = BN / NUM_CG;    // accumulator columns per epilogue warp
+  // columns per TMEM load (16 keeps the 768-thread kernel within its 80
+  // registers per thread without spills)
+  static constexpr int CHUNK = EPI_COLS < 16 ? EPI_COLS : 16;
   static constexpr int XH_OFF = BM * BK;
   static constexpr int XL_OFF = XH_OFF + BN * BK;
   static constexpr int STAGE_BYTES = XL_OFF + BN * BK;  // multiple of 1024 for BN % 8 == 0
   static constexpr int TMEM_COLS = NBUF * TCOLS <= 32 ? 32 : NBUF * TCOLS <= 64 ? 64 : NBUF * TCOLS <= 128 ? 128
                                    : NBUF * TCOLS <= 256 ? 256 : 512;
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-  // barriers: full[S], empty[S], tfull[NBUF], tempty[NBUF], done
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * NBUF + 1;
+  // barriers: full[S], empty[S], tfull[NBUF], tempty[NBUF], done, ufull[RING], uempty[RING]
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * NBUF + 1 + 2 * RING;
   static constexpr int MISC_OFF = BAR_OFF + 8 * NUM_BARS;
-  static constexpr int TABLE_OFF = ((MISC_OFF + 16 + 15) / 16) * 16;
-  // Of the per-group tables only the unit prefix sums (searched at every
-  // unit start) live in shared memory; the rest is read from global memory
-  // (L1-cached), so that shared memory goes to the stage ring.
-  static constexpr int SMEM_BYTES = TABLE_OFF + 4 * MAX_GROUPS + 1024;  // + alignment slack
-  static_assert(BN % 32 == 0 && BN <= 256 && EPI_COLS % CHUNK == 0 && NBUF * TCOLS <= 512 &&
-                    (!NCAT || 2 * BN <= 256), "tile shape");
+  static constexpr int PLAN_OFF = ((MISC_OFF + 16 + 15) / 16) * 16;
+  static constexpr int SMEM_BYTES = PLAN_OFF + RING * static_cast<int>(sizeof(UnitPlan)) + 1024;  // + alignment slack
+  static_assert(EPI_WARPS % 4 == 0 && BN % NUM_CG == 0, "epilogue split");
+  static_assert(EPI_COLS <= 32 && (CHUNK == 8 || CHUNK == 16) && EPI_COLS % CHUNK == 0, "epilogue columns");
+  static_assert(BN % 32 == 0 && BN <= 256 && NBUF * TCOLS <= 512 && (!NCAT || 2 * BN <= 256), "tile shape");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
-// unit -> (group, feature tile, token tile)
+// unit -> (group, feature tile, token tile), from the unit prefix sums
 template <int BN>
-__device__ __forceinline__ void decode_unit(int u, int n_groups, const int* ustart, const int* counts, int& g,
-                                            int& mt, int& nt) {
+__device__ __forceinline__ void decode_unit(int u, int n_groups, const int* __restrict__ ustart,
+                                            const int* __restrict__ counts, int& g, int& mt, int& nt) {
   int lo = 0, hi = n_groups;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (ustart[mid] <= u) lo = mid; else hi = mid;
+    if (__ldg(ustart + mid) <= u) lo = mid; else hi = mid;
   }
   g = lo;
-  const int ntiles = (counts[g] + BN - 1) / BN;
-  const int local = u - ustart[g];
+  const int ntiles = (__ldg(counts + g) + BN - 1) / BN;
+  const int local = u - __ldg(ustart + g);
   mt = local / ntiles;
   nt = local - mt * ntiles;
 }
 
-template <int BN_, int STAGES_, int NBUF_, bool NCAT_>
-__global__ void __maxnreg__(96)
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v) {
+  if constexpr (N == 16) tmem_ld16(taddr, v);
+  else tmem_ld8(taddr, v);
+}
+
+// Bring one weight tile (128 rows x 128 bytes) into L2 ahead of its TMA load.
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
+               : "memory");
+}
+
+template <int BN_, int STAGES_, int NBUF_, bool NCAT_, int EPI_WARPS_>
+__global__ void __launch_bounds__(Cfg<BN_, STAGES_, NBUF_, NCAT_, EPI_WARPS_>::NUM_THREADS, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_x32,
                     const GemmParams p) {
-  using C = Cfg<BN_, STAGES_, NBUF_, NCAT_>;
+  using C = Cfg<BN_, STAGES_, NBUF_, NCAT_, EPI_WARPS_>;
   constexpr int BN = C::BN;
   constexpr int STAGES = C::STAGES;
   constexpr int NBUF = C::NBUF;
@@ -123,18 +161,16 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + NBUF;
   uint64_t* done_bar = tempty + NBUF;
+  uint64_t* ufull = done_bar + 1;
+  uint64_t* uempty = ufull + RING;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
-  int* s_ustart = reinterpret_cast<int*>(smem + C::TABLE_OFF);
-  const int* __restrict__ s_counts = p.counts;
-  const int* __restrict__ s_rows = p.row_start;
-  const int* __restrict__ s_slot = p.slot_of;
+  UnitPlan* plan = reinterpret_cast<UnitPlan*>(smem + C::PLAN_OFF);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int NG = p.n_groups;
 
-  for (int i = threadIdx.x; i <= NG; i += blockDim.x) s_ustart[i] = p.unit_start[i];
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -142,9 +178,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], NUM_EPI_WARPS);
+      mbar_init(&tempty[b], C::EPI_WARPS);
     }
-    mbar_init(done_bar, NUM_MMA_ISSUERS);
+    mbar_init(done_bar, 2);
+    for (int r = 0; r < RING; ++r) {
+      mbar_init(&ufull[r], 32);                    // every lane of the planner warp
+      mbar_init(&uempty[r], 3 + C::EPI_WARPS);     // producer, two issuers, epilogue warps
+    }
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -160,14 +200,47 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   tc_fence_after();
 
   const uint32_t tmem_base = *s_tmem;
-  const int total_units = s_ustart[NG];
+  const int total_units = __ldg(p.unit_start + NG);
   const int n_kb = p.K / BK;
   // 128-row tiles per matrix; a ragged last tile (single-slot linear layers
   // such as 576 outputs) reads zero-filled rows past the end of the weight
   // and stores only rows < M.
   const int mt_per_mat = (p.M + BM - 1) / BM;
 
-  if (warp == 0) {
+  if (warp == PLAN_WARP) {
+    // ------------------------------------------------------------- planner
+    int i = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++i) {
+      int g, mt, nt;
+      decode_unit<BN>(u, NG, p.unit_start, p.counts, g, mt, nt);
+      const int slot = __ldg(p.slot_of + g);
+      if (slot < 0 || slot >= p.n_slots) {
+        if (lane == 0) atomicCAS(p.status, 0, kDevBadSlot);
+        *s_abort = 1;  // every role leaves its next wait
+        break;
+      }
+      const int mat = mt >= mt_per_mat;
+      const int mtl = mt - mat * mt_per_mat;
+      const int wsc_off = (slot * mt_per_mat + mtl) * n_kb;
+      const float swv = lane < n_kb ? __ldg((mat ? p.wscale1 : p.wscale0) + wsc_off + lane) : 0.f;
+      const int ncols = min(BN, __ldg(p.counts + g) - nt * BN);
+      const int row0 = __ldg(p.row_start + g) + nt * BN;
+      const int ri = i % RING;
+      if (!mbar_wait(&uempty[ri], ((i / RING) & 1) ^ 1, p.status, kDevTimeoutProducer, s_abort)) break;
+      UnitPlan* e = plan + ri;
+      if (lane == 0) {
+        e->ncols = ncols;
+        e->row0 = row0;
+        e->wrow = slot * p.M + mtl * BM;
+        e->mat = mat;
+        e->mrow = mtl * BM;
+        e->nmma = C::NCAT ? 2 * BN : (ncols + 15) & ~15;
+        e->wsc_off = wsc_off;
+      }
+      e->sw[lane] = swv;
+      mbar_arrive(&ufull[ri]);  // each lane publishes its own writes
+    }
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
@@ -175,26 +248,34 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
+      int pf_done = 0;  // K steps of the current unit already prefetched into L2
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        int g, mt, nt;
-        decode_unit<BN>(u, NG, s_ustart, s_counts, g, mt, nt);
-        const int slot = s_slot[g];
-        if (slot < 0 || slot >= p.n_slots) {
-          atomicCAS(p.status, 0, kDevBadSlot);
-          *s_abort = 1;
-          break;
+      int i = 0;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++i) {
+        const int ri = i % RING;
+        if (!mbar_wait(&ufull[ri], (i / RING) & 1, p.status, kDevTimeoutProducer, s_abort)) break;
+        const UnitPlan* e = plan + ri;
+        const int ncols = e->ncols, row0 = e->row0, wrow = e->wrow, mat = e->mat;
+        // The next unit's weight rows, when its plan is already there (no
+        // wait), for the L2 prefetch that runs past the end of this unit. Its
+        // entry cannot be reused before this thread releases it.
+        int nwrow = -1, nmat = 0;
+        if (u + static_cast<int>(gridDim.x) < total_units) {
+          const int rn = (i + 1) % RING;
+          if (mbar_try_wait(&ufull[rn], ((i + 1) / RING) & 1)) {
+            nwrow = plan[rn].wrow;
+            nmat = plan[rn].mat;
+          }
         }
-        const int mat = mt >= mt_per_mat;
+        mbar_arrive(&uempty[ri]);
         const CUtensorMap* tw = mat ? &tm_w1 : &tm_w0;
-        const int col0 = nt * BN;
-        const int ncols = min(BN, s_counts[g] - col0);
+        const CUtensorMap* twn = nmat ? &tm_w1 : &tm_w0;
+        for (int kb = pf_done; kb < PF_DIST && kb < n_kb; ++kb) tma_prefetch_l2(tw, kb * BK, wrow);
+        int next_pf = 0;
         const int nsub = (ncols + SUB - 1) / SUB;
         // A few 32-row boxes beat one big box; four or more cost more than the
         // rows they save (a 128-token tile as 4 boxes: +8% kernel time).
         const bool small = BN == SUB || (nsub * SUB < BN && nsub <= 2);
-        const int row0 = s_rows[g] + col0;
-        const int wrow = slot * p.M + (mt - mat * mt_per_mat) * BM;
         const uint32_t bytes = BM * BK + 2 * (small ? nsub * SUB : BN) * BK;
         for (int kb = 0; kb < n_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kDevTimeoutProducer, s_abort)) { ok = false; break; }
@@ -211,33 +292,42 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
             tma_load_2d(st + C::XH_OFF, &tm_x, &full[stage], kb * BK, row0, pol_x);
             tma_load_2d(st + C::XL_OFF, &tm_x, &full[stage], kb * BK, p.P + row0, pol_x);
           }
+          const int pk = kb + PF_DIST;
+          if (pk < n_kb) {
+            tma_prefetch_l2(tw, pk * BK, wrow);
+          } else if (nwrow >= 0 && pk - n_kb < n_kb) {
+            tma_prefetch_l2(twn, (pk - n_kb) * BK, nwrow);
+            next_pf = pk - n_kb + 1;
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
+        pf_done = next_pf;
       }
       // Drain: the copies of the last issued stages must have landed before
       // the CTA may exit (normally they were consumed already).
       const int n_drain = issued < STAGES ? issued : STAGES;
-      for (int i = 0; i < n_drain; ++i) {
+      for (int d = 0; d < n_drain; ++d) {
         if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
         mbar_wait(&full[stage], phase, p.status, kDevTimeoutProducer, s_abort);
       }
     }
-  } else if (warp == 1 || warp == ISSUER_B_WARP) {
+  } else if (warp == 1 || warp == 2) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
-      const int me = warp == 1 ? 0 : 1;  // issues the K steps of this parity
+      const int me = warp - 1;  // issues the K steps of this parity
       int step = 0;
       int stage = 0;
       uint32_t phase = 0;
       int tb = 0;
       uint32_t tphase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        int g, mt, nt;
-        decode_unit<BN>(u, NG, s_ustart, s_counts, g, mt, nt);
-        const int ncols = min(BN, s_counts[g] - nt * BN);
-        const int N = C::NCAT ? 2 * BN : (ncols + 15) & ~15;
+      int i = 0;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++i) {
+        const int ri = i % RING;
+        if (!mbar_wait(&ufull[ri], (i / RING) & 1, p.status, kDevTimeoutMma, s_abort)) break;
+        const int N = plan[ri].nmma;
+        mbar_arrive(&uempty[ri]);
         const uint32_t idesc = idesc_e4m3(BM, N);
         for (int kb = 0; kb < n_kb; ++kb, ++step) {
           if ((step & 1) != me) {  // the other issuer's step: only advance the rings
@@ -276,47 +366,46 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       mma_commit(done_bar);
       mbar_wait(done_bar, 0, p.status, kDevTimeoutMma, s_abort);
     }
-  } else if (warp >= 2 && warp < 2 + NUM_EPI_WARPS) {
+  } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;
-    const int cg = (warp - 2) >> 2;
+    const int quad = warp & 3;  // a warp reads the TMEM lanes of quadrant warp % 4
+    const int cg = (warp - EPI_WARP0) >> 2;
     const int c0 = cg * EPI_COLS;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const int out_ld = p.n_mat * p.M;
     int tb = 0;
     uint32_t tphase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-      int g, mt, nt;
-      decode_unit<BN>(u, NG, s_ustart, s_counts, g, mt, nt);
-      const int slot = s_slot[g];
-      const int ncols = min(BN, s_counts[g] - nt * BN);
+    int i = 0;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++i) {
+      const int ri = i % RING;
+      if (!mbar_wait(&ufull[ri], (i / RING) & 1, p.status, kDevTimeoutEpilogue, s_abort)) break;
+      const UnitPlan* e = plan + ri;
+      const int ncols = e->ncols, row0 = e->row0, mat = e->mat, mrow = e->mrow, wsc_off = e->wsc_off;
+      // Weight block scales, one per K block, in 32-block windows: lane i
+      // holds kb = 32w + i of window w in register w % 2; window 0 comes from
+      // the plan, entering window w refills the other register with window
+      // w + 1 from global memory, 32 K steps before it is needed.
+      float swr0 = e->sw[lane];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&uempty[ri]);
+      const float* wsc = (mat ? p.wscale1 : p.wscale0) + wsc_off;
+      float swr1 = 32 + lane < n_kb ? __ldg(wsc + 32 + lane) : 0.f;
       const int nvalid = max(0, min(EPI_COLS, ncols - c0));  // valid columns of this warp
-      const int mat = mt >= mt_per_mat;
-      // Weight block scales of this unit's 128-row tile, one per K block, in
-      // two 32-block windows: lane i holds kb = 32w + i of window w in
-      // register w % 2; entering window w refills the other register with
-      // window w + 1, 32 K steps before it is needed.
-      const bool slot_ok = slot >= 0 && slot < p.n_slots;  // the producer reports a bad slot
-      const float* wsc = (mat ? p.wscale1 : p.wscale0) +
-                         (static_cast<size_t>(slot_ok ? slot : 0) * mt_per_mat + (mt - mat * mt_per_mat)) * n_kb;
-      float swr0 = slot_ok && lane < n_kb ? __ldg(wsc + lane) : 0.f;
-      float swr1 = slot_ok && 32 + lane < n_kb ? __ldg(wsc + 32 + lane) : 0.f;
-      // Per-row activation scales of this warp's columns (lane i holds column
-      // i and 32 + i), loaded now so that the latency hides behind the K loop.
-      const int row_base = s_rows[g] + nt * BN + c0;
-      const float sxa = lane < nvalid ? __ldg(p.sx + row_base + lane) : 0.f;
-      const float sxb = 32 + lane < nvalid ? __ldg(p.sx + row_base + 32 + lane) : 0.f;
+      // Per-row activation scale of this warp's column `lane`, loaded now so
+      // that the latency hides behind the K loop.
+      const int row_base = row0 + c0;
+      const float sxv = lane < nvalid ? __ldg(p.sx + row_base + lane) : 0.f;
       float acc[EPI_COLS];
 #pragma unroll
-      for (int i = 0; i < EPI_COLS; ++i) acc[i] = 0.f;
+      for (int c = 0; c < EPI_COLS; ++c) acc[c] = 0.f;
 
       for (int kb = 0; kb < n_kb; ++kb) {
         if (!mbar_wait(&tfull[tb], tphase, p.status, kDevTimeoutEpilogue, s_abort)) { ok = false; break; }
         tc_fence_after();
         if ((kb & 31) == 0 && kb >= 32) {
           const int nk = kb + 32 + lane;
-          const float v = slot_ok && nk < n_kb ? __ldg(wsc + nk) : 0.f;
+          const float v = nk < n_kb ? __ldg(wsc + nk) : 0.f;
           if ((kb >> 5) & 1) swr0 = v; else swr1 = v;
         }
         const float sw = __shfl_sync(0xffffffffu, ((kb >> 5) & 1) ? swr1 : swr0, kb & 31);
@@ -325,24 +414,21 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
           if (q * CHUNK < nvalid) {  // warp-uniform
             const uint32_t ta = tmem_base + lane_base + tb * C::TCOLS + c0 + q * CHUNK;
             float part[CHUNK];
-            if constexpr (CHUNK == 16) tmem_ld16(ta, part);
-            else tmem_ld8(ta, part);
+            tmem_ld<CHUNK>(ta, part);
             if constexpr (C::NCAT) {
               float lo[CHUNK];
-              if constexpr (CHUNK == 16) tmem_ld16(ta + BN, lo);
-              else tmem_ld8(ta + BN, lo);
+              tmem_ld<CHUNK>(ta + BN, lo);
               tmem_ld_wait();
 #pragma unroll
-              for (int i = 0; i < CHUNK; ++i) part[i] += lo[i];
+              for (int c = 0; c < CHUNK; ++c) part[c] += lo[c];
             } else {
               tmem_ld_wait();
             }
             // Packed fp32x2 FMAs: half the issue slots of scalar fmaf, same
-            // rounding (-2% kernel time at T=4096, where the GEMM runs at
-            // the power cap).
+            // rounding.
 #pragma unroll
-            for (int i = 0; i < CHUNK; i += 2)
-              fma2(acc[q * CHUNK + i], acc[q * CHUNK + i + 1], part[i], part[i + 1], sw);
+            for (int c = 0; c < CHUNK; c += 2)
+              fma2(acc[q * CHUNK + c], acc[q * CHUNK + c + 1], part[c], part[c + 1], sw);
           }
         }
         tc_fence_before();
@@ -351,25 +437,25 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         if (++tb == NBUF) { tb = 0; tphase ^= 1; }
       }
       if (!ok) break;
-      // Stores of bf16 pairs: for tokens i and i+1, an even lane writes
-      // features (lane, lane+1) of token i and its odd neighbour features
-      // (lane-1, lane) of token i+1; one shuffle exchanges the halves.
+      // Stores of bf16 pairs: for tokens c and c+1, an even lane writes
+      // features (lane, lane+1) of token c and its odd neighbour features
+      // (lane-1, lane) of token c+1; one shuffle exchanges the halves.
       const int odd = lane & 1;
-      const int row_in_mat = (mt - mat * mt_per_mat) * BM + quad * 32 + (lane & ~1);  // the pair's first row
+      const int row_in_mat = mrow + quad * 32 + (lane & ~1);  // the pair's first row
       const bool row_ok = row_in_mat < p.M;  // M is even: the pair is inside or outside together
       __nv_bfloat16* ybase = p.y + mat * p.M + row_in_mat;
 #pragma unroll
-      for (int i = 0; i < EPI_COLS; i += 2) {
-        const float s0 = __shfl_sync(0xffffffffu, i < 32 ? sxa : sxb, i & 31);
-        const float s1 = __shfl_sync(0xffffffffu, i + 1 < 32 ? sxa : sxb, (i + 1) & 31);
-        const __nv_bfloat16 v0 = __float2bfloat16_rn(acc[i] * s0);
-        const __nv_bfloat16 v1 = __float2bfloat16_rn(acc[i + 1] * s1);
+      for (int c = 0; c < EPI_COLS; c += 2) {
+        const float s0 = __shfl_sync(0xffffffffu, sxv, c);
+        const float s1 = __shfl_sync(0xffffffffu, sxv, c + 1);
+        const __nv_bfloat16 v0 = __float2bfloat16_rn(acc[c] * s0);
+        const __nv_bfloat16 v1 = __float2bfloat16_rn(acc[c + 1] * s1);
         const unsigned short mine = __bfloat16_as_ushort(odd ? v1 : v0);
         const unsigned short other = static_cast<unsigned short>(
             __shfl_xor_sync(0xffffffffu, static_cast<unsigned int>(__bfloat16_as_ushort(odd ? v0 : v1)), 1));
         const uint32_t pair = odd ? (static_cast<uint32_t>(other) | (static_cast<uint32_t>(mine) << 16))
                                   : (static_cast<uint32_t>(mine) | (static_cast<uint32_t>(other) << 16));
-        const int tok = i + odd;
+        const int tok = c + odd;
         if (tok < nvalid && row_ok)
           *reinterpret_cast<uint32_t*>(ybase + static_cast<size_t>(row_base + tok) * out_ld) = pair;
       }
@@ -382,22 +468,23 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
   if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
-template <int BN, int STAGES, int NBUF, bool NCAT>
+template <int BN, int STAGES, int NBUF, bool NCAT, int EPI_WARPS>
 cudaError_t launch_cfg(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x, const CUtensorMap& x32,
                        const GemmParams& p, int grid, cudaStream_t stream) {
-  using C = Cfg<BN, STAGES, NBUF, NCAT>;
+  using C = Cfg<BN, STAGES, NBUF, NCAT, EPI_WARPS>;
   static bool attr[64] = {false};
   int dev = 0;
   const cudaError_t de = cudaGetDevice(&dev);
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, NBUF, NCAT>,
+    cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, NBUF, NCAT, EPI_WARPS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  grouped_gemm_kernel<BN, STAGES, NBUF, NCAT><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(w0, w1, x, x32, p);
+  grouped_gemm_kernel<BN, STAGES, NBUF, NCAT, EPI_WARPS>
+      <<<grid, C::NUM_THREADS, C::SMEM_BYTES, stream>>>(w0, w1, x, x32, p);
   return cudaGetLastError();
 }
 
@@ -417,10 +504,10 @@ cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, co
   if (p.n_groups > gg::MAX_GROUPS - 1 || (p.n_mat != 1 && p.n_mat != 2))
     return cudaErrorInvalidValue;
   switch (tile) {
-    case 32: return gg::launch_cfg<32, 8, 8, true>(w0, w1, x, x32, p, grid, stream);
-    case 64: return gg::launch_cfg<64, 6, 4, true>(w0, w1, x, x32, p, grid, stream);
-    case 128: return gg::launch_cfg<128, 4, 2, true>(w0, w1, x, x32, p, grid, stream);
-    case 160: return gg::launch_cfg<160, 4, 3, false>(w0, w1, x, x32, p, grid, stream);
+    case 32: return gg::launch_cfg<32, 8, 8, true, 16>(w0, w1, x, x32, p, grid, stream);
+    case 64: return gg::launch_cfg<64, 6, 4, true, 16>(w0, w1, x, x32, p, grid, stream);
+    case 128: return gg::launch_cfg<128, 4, 2, true, 16>(w0, w1, x, x32, p, grid, stream);
+    case 160: return gg::launch_cfg<160, 4, 3, false, 20>(w0, w1, x, x32, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
