@@ -104,7 +104,7 @@ int num_sms() {
 
 // --------------------------------------------------------------- workspace
 struct Ws {
-  size_t status = 0, counts = 0, cursor = 0, row_start = 0, us_up = 0, us_dn = 0, slot0 = 0;
+  size_t status = 0, counts = 0, cursor = 0, row_start = 0, us_up = 0, us_dn = 0, slot0 = 0, nrows = 0;
   size_t partial = 0, idx = 0, w = 0, pos = 0, xq = 0, sx = 0, gu = 0, hq = 0, hs = 0, y = 0, total = 0;
   int P = 0, ksplit = 1, NG = 1, tile = 32;
 };
@@ -128,6 +128,7 @@ Ws plan_moe(int T, int H, int F, int E, int K) {
   w.us_up = take(4 * (w.NG + 1));
   w.us_dn = take(4 * (w.NG + 1));
   w.slot0 = take(4);
+  w.nrows = take(4);
   w.partial = take(sizeof(float) * static_cast<size_t>(w.ksplit) * T * E);
   w.idx = take(4 * static_cast<size_t>(pairs));
   w.w = take(4 * static_cast<size_t>(pairs));
@@ -611,10 +612,14 @@ size_t dsmoe_moe_local_workspace_size(const dsmoe_moe_config_t* cfg, int32_t row
   return plan_moe(rows, cfg->hidden, cfg->inter, cfg->n_routed, cfg->top_k).total;
 }
 
+// rows_from (optional, peer-memory step): counts_all [world][world] on the
+// device; the rows actually received are sum_s counts_all[s][me], counted on
+// the device, and `rows` is only the bound that sizes the workspace and grids.
 static int moe_local_impl(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* hidden,
                           int32_t rows, const int32_t* local_idx, const float* local_w, void* partial_out,
                           const int32_t* origin, const uint64_t* peer_out, int me, int cap, void* workspace,
-                          size_t workspace_bytes, dsmoe_stream_t stream) {
+                          size_t workspace_bytes, dsmoe_stream_t stream, const int32_t* rows_from = nullptr,
+                          int world = 1) {
   int r = check_cfg(cfg);
   if (r) return r;
   if ((r = check_weights(cfg, w))) return r;
@@ -632,18 +637,23 @@ static int moe_local_impl(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weigh
   int32_t* counts = at<int32_t>(ws, L.counts);
   int32_t* row_start = at<int32_t>(ws, L.row_start);
   int32_t* pos = at<int32_t>(ws, L.pos);
-  DSMOE_CUDA(launch_count(local_idx, rows * K, counts, NG, s));
+  int32_t* nrows = nullptr;
+  if (rows_from) {
+    nrows = at<int32_t>(ws, L.nrows);
+    DSMOE_CUDA(launch_ep_recv_rows(rows_from, world, me, nrows, s));
+  }
+  DSMOE_CUDA(launch_count(local_idx, rows * K, counts, NG, s, nrows, K));
   DSMOE_CUDA(launch_plan(counts, NG, 0, L.tile, 2 * F / 128, H / 128, row_start, at<int32_t>(ws, L.cursor),
                          at<int32_t>(ws, L.us_up), at<int32_t>(ws, L.us_dn), s));
   DSMOE_CUDA(launch_quant_scatter(hidden, rows, H, local_idx, K, NG, 0, row_start, at<int32_t>(ws, L.cursor), L.P,
-                                  at<uint8_t>(ws, L.xq), at<float>(ws, L.sx), pos, s));
+                                  at<uint8_t>(ws, L.xq), at<float>(ws, L.sx), pos, s, nrows));
   prof(2, s);
   __nv_bfloat16* y = at<__nv_bfloat16>(ws, L.y);
   if ((r = run_ffn(w->w_gate, w->s_gate, w->w_up, w->s_up, w->w_down, w->s_down, w->n_slots, H, F, L, ws,
                    w->slot_of_expert, NG, y, s)))
     return r;
   DSMOE_CUDA(launch_combine(y, rows, H, pos, local_w, K, row_start, 1.0f, 0, nullptr,
-                            static_cast<__nv_bfloat16*>(partial_out), s, origin, peer_out, me, cap));
+                            static_cast<__nv_bfloat16*>(partial_out), s, origin, peer_out, me, cap, nrows));
   prof(6, s);
   return DSMOE_OK;
 }
@@ -677,7 +687,7 @@ int dsmoe_ep_plan(const int64_t* topk_idx, const float* topk_w, int32_t tokens, 
 int dsmoe_ep_push(const void* hidden, int32_t tokens, int32_t top_k, int32_t hidden_size, int32_t world, int32_t rank,
                   int32_t cap, const int32_t* counts_all, const int32_t* send_tok, const int32_t* send_idx,
                   const float* send_w, int32_t* tok_rows, const uint64_t* peer_recv_hidden,
-                  const uint64_t* peer_recv_meta, dsmoe_stream_t stream) {
+                  const uint64_t* peer_recv_meta, int32_t* device_status, int32_t max_blocks, dsmoe_stream_t stream) {
   if (tokens < 0 || top_k < 1 || top_k > 8 || world < 1 || world > 64 || rank < 0 || rank >= world ||
       hidden_size <= 0 || hidden_size % 8 || cap < tokens)
     return fail(DSMOE_ERR_INVALID, "ep_push: bad sizes (tokens %d, cap %d, rank %d of %d)", tokens, cap, rank, world);
@@ -687,13 +697,15 @@ int dsmoe_ep_push(const void* hidden, int32_t tokens, int32_t top_k, int32_t hid
     if (!p) return fail(DSMOE_ERR_INVALID, "ep_push: NULL pointer");
   if (!aligned16(hidden)) return fail(DSMOE_ERR_INVALID, "ep_push: unaligned rows");
   DSMOE_CUDA(launch_ep_push(hidden, tokens, hidden_size, top_k, world, rank, cap, counts_all, send_tok, send_idx,
-                            send_w, tok_rows, peer_recv_hidden, peer_recv_meta, reinterpret_cast<cudaStream_t>(stream)));
+                            send_w, tok_rows, peer_recv_hidden, peer_recv_meta, reinterpret_cast<int*>(device_status),
+                            max_blocks, reinterpret_cast<cudaStream_t>(stream)));
   return DSMOE_OK;
 }
 
 int dsmoe_moe_local_peer(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* w, const void* recv_hidden,
                          int32_t rows, const int32_t* recv_meta, int32_t world, int32_t rank, int32_t cap,
-                         const uint64_t* peer_return, void* workspace, size_t workspace_bytes, dsmoe_stream_t stream) {
+                         const uint64_t* peer_return, const int32_t* counts_all, void* workspace,
+                         size_t workspace_bytes, dsmoe_stream_t stream) {
   if (world < 1 || world > 64 || rank < 0 || rank >= world || cap < 1 || rows < 0 ||
       static_cast<int64_t>(rows) > static_cast<int64_t>(world) * cap)
     return fail(DSMOE_ERR_INVALID, "moe_local_peer: bad sizes (rows %d, cap %d, rank %d of %d)", rows, cap, rank,
@@ -707,7 +719,7 @@ int dsmoe_moe_local_peer(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weight
   const float* wts = reinterpret_cast<const float*>(recv_meta + cap_rows * K);
   const int32_t* origin = recv_meta + 2 * cap_rows * K;
   return moe_local_impl(cfg, w, recv_hidden, rows, idx, wts, nullptr, origin, peer_return, rank, cap, workspace,
-                        workspace_bytes, stream);
+                        workspace_bytes, stream, counts_all, world);
 }
 
 size_t dsmoe_ep_meta_bytes(int32_t world, int32_t cap, int32_t top_k) {

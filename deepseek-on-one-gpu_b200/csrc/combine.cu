@@ -30,8 +30,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
                                                       int has_shared, const __nv_bfloat16* __restrict__ residual,
                                                       __nv_bfloat16* __restrict__ out,
                                                       const int32_t* __restrict__ origin,
-                                                      const uint64_t* __restrict__ peer_out, int me, int cap) {
+                                                      const uint64_t* __restrict__ peer_out, int me, int cap,
+                                                      const int32_t* __restrict__ n_rows) {
   const int t = blockIdx.x;
+  if (n_rows && t >= *n_rows) return;  // rows beyond the device-side count (whole CTA)
   __shared__ int s_row[8];
   __shared__ __nv_bfloat162 s_w2[8];  // bf16(w[t,k]) in both halves
   if (threadIdx.x < top_k) {
@@ -105,10 +107,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
                            const int32_t* row_start, float scale, int has_shared, const __nv_bfloat16* residual,
                            __nv_bfloat16* out, cudaStream_t stream, const int32_t* origin, const uint64_t* peer_out,
-                           int me, int cap) {
+                           int me, int cap, const int32_t* n_rows) {
   if (T == 0) return cudaSuccess;
   cb::combine_kernel<<<T, 256, 0, stream>>>(y, T, H, pos, w, top_k, row_start, scale, has_shared, residual, out,
-                                            origin, peer_out, me, cap);
+                                            origin, peer_out, me, cap, n_rows);
 
   return cudaGetLastError();
 }

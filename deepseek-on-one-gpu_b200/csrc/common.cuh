@@ -27,6 +27,7 @@ enum DevErr : int {
   kDevTimeoutEpilogue = 3,
   kDevBadSlot = 4,
   kDevBadExpert = 5,
+  kDevBadCount = 6,  // exchange counts inconsistent with the receive buffers
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

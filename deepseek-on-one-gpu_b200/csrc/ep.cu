@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(256) push_kernel(const __nv_bfloat16* __restri
                                                    const int32_t* __restrict__ send_idx,
                                                    const float* __restrict__ send_w, int32_t* __restrict__ tok_rows,
                                                    const uint64_t* __restrict__ recv_x,
-                                                   const uint64_t* __restrict__ recv_meta) {
+                                                   const uint64_t* __restrict__ recv_meta, int* __restrict__ status) {
   __shared__ int s_lbase[MAX_WORLD + 1];  // this rank's rows before destination d
   __shared__ int s_rbase[MAX_WORLD];      // rows lower ranks send to d
   if (threadIdx.x == 0) {
@@ -156,8 +156,16 @@ __global__ void __launch_bounds__(256) push_kernel(const __nv_bfloat16* __restri
     while (d + 1 < W && s_lbase[d + 1] <= r) ++d;
     const int k = r - s_lbase[d];
     const size_t p = static_cast<size_t>(s_rbase[d]) + k;
-    if (k >= cap || p >= cap_rows) continue;  // counts inconsistent with the buffers: write nothing
     const int t = send_tok[r];
+    if (k >= cap || p >= cap_rows) {
+      // counts inconsistent with the buffers: write nothing, drop the row from
+      // the combine and record the error
+      if (threadIdx.x == 0) {
+        tok_rows[static_cast<size_t>(t) * W + d] = -1;
+        if (status) atomicCAS(status, 0, kDevBadCount);
+      }
+      continue;
+    }
     const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H);
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(recv_x[d]) + p * H);
     for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = __ldg(src + c);
@@ -173,6 +181,16 @@ __global__ void __launch_bounds__(256) push_kernel(const __nv_bfloat16* __restri
     }
   }
   __threadfence_system();
+}
+
+// Rows this rank receives in a peer-memory step: sum over source ranks s of
+// counts_all[s][me] (one warp).
+__global__ void recv_rows_kernel(const int32_t* __restrict__ counts_all, int W, int me, int32_t* __restrict__ out) {
+  int v = 0;
+  for (int s = threadIdx.x; s < W; s += 32) v += counts_all[s * W + me];
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (threadIdx.x == 0) *out = v;
 }
 
 // out[t] = bf16(shared[t] + bf16(scale * acc)), acc = bf16 sum of the
@@ -238,13 +256,21 @@ cudaError_t launch_ep_plan(const int64_t* idx, const float* w, int T, int K, int
 
 cudaError_t launch_ep_push(const void* x, int T, int H, int K, int W, int me, int cap, const int32_t* counts_all,
                            const int32_t* send_tok, const int32_t* send_idx, const float* send_w, int32_t* tok_rows,
-                           const uint64_t* recv_x, const uint64_t* recv_meta, cudaStream_t stream) {
+                           const uint64_t* recv_x, const uint64_t* recv_meta, int* status, int max_blocks,
+                           cudaStream_t stream) {
   if (W < 1 || W > ep::MAX_WORLD || me < 0 || me >= W || K > 8) return cudaErrorInvalidValue;
   int blocks = T * (K < W ? K : W);
   if (blocks > 4096) blocks = 4096;
+  if (max_blocks > 0 && blocks > max_blocks) blocks = max_blocks;
   if (blocks < 1) blocks = 1;
   ep::push_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), H, K, W, me, cap, counts_all,
-                                              send_tok, send_idx, send_w, tok_rows, recv_x, recv_meta);
+                                              send_tok, send_idx, send_w, tok_rows, recv_x, recv_meta, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_recv_rows(const int32_t* counts_all, int W, int me, int32_t* out, cudaStream_t stream) {
+  if (W < 1 || W > ep::MAX_WORLD || me < 0 || me >= W) return cudaErrorInvalidValue;
+  ep::recv_rows_kernel<<<1, 32, 0, stream>>>(counts_all, W, me, out);
   return cudaGetLastError();
 }
 

@@ -55,13 +55,16 @@ cudaError_t launch_router_select(const float* partial, int ksplit, const float* 
                                  int64_t* idx64, float* w, cudaStream_t stream);
 
 // Permutation (permute.cu)
-cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream);
+// n_rows (optional): a row count held on the device; work past it is skipped
+// (n_pairs / T are then bounds that size the grids).
+cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream,
+                         const int32_t* n_rows = nullptr, int per_row = 1);
 cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int tile, int mt_up, int mt_dn,
                         int32_t* row_start, int32_t* cursor, int32_t* ustart_up, int32_t* ustart_dn,
                         cudaStream_t stream);
 cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int n_groups,
                                  int has_shared, const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq,
-                                 float* sx, int32_t* pos, cudaStream_t stream);
+                                 float* sx, int32_t* pos, cudaStream_t stream, const int32_t* n_rows = nullptr);
 
 // Combine (combine.cu)
 // residual (optional, [T][H]): out = bf16(residual + combined row)
@@ -69,7 +72,8 @@ cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx
 cudaError_t launch_combine(const __nv_bfloat16* y, int T, int H, const int32_t* pos, const float* w, int top_k,
                            const int32_t* row_start, float scale, int has_shared, const __nv_bfloat16* residual,
                            __nv_bfloat16* out, cudaStream_t stream, const int32_t* origin = nullptr,
-                           const uint64_t* peer_out = nullptr, int me = 0, int cap = 0);
+                           const uint64_t* peer_out = nullptr, int me = 0, int cap = 0,
+                           const int32_t* n_rows = nullptr);
 
 // y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), one row of H per token
 cudaError_t launch_rmsnorm(const void* x, const void* w, float eps, int T, int H, void* y, cudaStream_t stream);
@@ -85,9 +89,14 @@ cudaError_t launch_ep_dispatch(const int64_t* idx, const float* w, const void* x
                                float* send_w, void* send_x, cudaStream_t stream);
 cudaError_t launch_ep_plan(const int64_t* idx, const float* w, int T, int K, int W, int El, int32_t* counts,
                            int32_t* tok_rows, int32_t* send_tok, int32_t* send_idx, float* send_w, cudaStream_t stream);
+// status (optional): device error word for rows whose counts do not fit the
+// receive buffers; max_blocks > 0 caps the grid (SMs left to concurrent work).
 cudaError_t launch_ep_push(const void* x, int T, int H, int K, int W, int me, int cap, const int32_t* counts_all,
                            const int32_t* send_tok, const int32_t* send_idx, const float* send_w, int32_t* tok_rows,
-                           const uint64_t* recv_x, const uint64_t* recv_meta, cudaStream_t stream);
+                           const uint64_t* recv_x, const uint64_t* recv_meta, int* status, int max_blocks,
+                           cudaStream_t stream);
+// *out = sum over s of counts_all[s][me]
+cudaError_t launch_ep_recv_rows(const int32_t* counts_all, int W, int me, int32_t* out, cudaStream_t stream);
 cudaError_t launch_ep_combine(const void* part, const int32_t* tok_rows, int T, int W, int H, const void* shared,
                               float scale, void* out, cudaStream_t stream);
 

@@ -24,10 +24,14 @@ namespace dsmoe {
 namespace pm {
 constexpr int MAX_GROUPS = 512;
 
+// n_rows (optional): the row count on the device; only its first
+// n_rows * per_row pairs are counted (n_pairs is the bound the grid covers).
 __global__ void __launch_bounds__(256) count_kernel(const int32_t* __restrict__ idx, int n_pairs,
-                                                    int32_t* __restrict__ counts, int n_groups) {
+                                                    int32_t* __restrict__ counts, int n_groups,
+                                                    const int32_t* __restrict__ n_rows, int per_row) {
   __shared__ int hist[MAX_GROUPS];
   for (int i = threadIdx.x; i < n_groups; i += blockDim.x) hist[i] = 0;
+  if (n_rows) n_pairs = min(n_pairs, *n_rows * per_row);
   __syncthreads();
   for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n_pairs; p += gridDim.x * blockDim.x) {
     const int g = idx[p] + 1;
@@ -122,8 +126,10 @@ __global__ void __launch_bounds__(QS_THREADS) quant_scatter_kernel(const __nv_bf
                                                                    const int32_t* __restrict__ row_start,
                                                                    int32_t* __restrict__ cursor, int P,
                                                                    uint8_t* __restrict__ xq, float* __restrict__ sx,
-                                                                   int32_t* __restrict__ pos) {
+                                                                   int32_t* __restrict__ pos,
+                                                                   const int32_t* __restrict__ n_rows) {
   const int t = blockIdx.x;
+  if (n_rows && t >= *n_rows) return;  // rows beyond the device-side count (whole CTA)
   __shared__ int s_rows[9];
   __shared__ float s_red[QS_THREADS / 32];
   const int tid = threadIdx.x;
@@ -195,14 +201,15 @@ __global__ void __launch_bounds__(QS_THREADS) quant_scatter_kernel(const __nv_bf
 }
 }  // namespace pm
 
-cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream) {
+cudaError_t launch_count(const int32_t* idx, int n_pairs, int32_t* counts, int n_groups, cudaStream_t stream,
+                         const int32_t* n_rows, int per_row) {
   if (n_groups > pm::MAX_GROUPS) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * n_groups, stream);
   if (e != cudaSuccess) return e;
   if (n_pairs == 0) return cudaSuccess;
   int blocks = (n_pairs + 255) / 256;
   if (blocks > 296) blocks = 296;
-  pm::count_kernel<<<blocks, 256, 0, stream>>>(idx, n_pairs, counts, n_groups);
+  pm::count_kernel<<<blocks, 256, 0, stream>>>(idx, n_pairs, counts, n_groups, n_rows, per_row);
   return cudaGetLastError();
 }
 
@@ -217,12 +224,12 @@ cudaError_t launch_plan(int32_t* counts, int n_groups, int shared_tokens, int ti
 
 cudaError_t launch_quant_scatter(const void* x, int T, int H, const int32_t* idx, int top_k, int n_groups,
                                  int has_shared, const int32_t* row_start, int32_t* cursor, int P, uint8_t* xq,
-                                 float* sx, int32_t* pos, cudaStream_t stream) {
+                                 float* sx, int32_t* pos, cudaStream_t stream, const int32_t* n_rows) {
   if (T == 0) return cudaSuccess;
   if (top_k + has_shared > 9) return cudaErrorInvalidValue;
   pm::quant_scatter_kernel<<<T, pm::QS_THREADS, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, idx,
                                                               top_k, n_groups, has_shared, row_start, cursor, P, xq,
-                                                              sx, pos);
+                                                              sx, pos, n_rows);
   return cudaGetLastError();
 }
 

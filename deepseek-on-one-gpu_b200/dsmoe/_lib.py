@@ -91,8 +91,8 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_moe_layer_ffn_workspace_size.restype = sz
                 L.dsmoe_moe_layer_ffn.argtypes = [cfgp, wp, vp, vp, ctypes.c_float, i32, vp, vp, vp, vp, sz, vp]
                 L.dsmoe_ep_plan.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
-                L.dsmoe_ep_push.argtypes = [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]
-                L.dsmoe_moe_local_peer.argtypes = [cfgp, wp, vp, i32, vp, i32, i32, i32, vp, vp, sz, vp]
+                L.dsmoe_ep_push.argtypes = [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, i32, vp]
+                L.dsmoe_moe_local_peer.argtypes = [cfgp, wp, vp, i32, vp, i32, i32, i32, vp, vp, vp, sz, vp]
                 L.dsmoe_ep_meta_bytes.argtypes = [i32, i32, i32]
                 L.dsmoe_ep_meta_bytes.restype = sz
                 L.dsmoe_ipc_alloc.argtypes = [sz, ctypes.POINTER(vp), vp]

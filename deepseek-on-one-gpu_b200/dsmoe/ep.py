@@ -39,6 +39,10 @@ destination rank's receive buffer, and the combine of ``dsmoe_moe_local_peer``
 writes each partial row straight into its origin rank's return buffer. Only
 the per-rank counts are gathered (NCCL all-gather of W ints) and two tiny
 all-reduces act as stream-ordered barriers between the writes and the reads.
+The host never reads a count: the rows a rank receives are summed from the
+gathered counts on the device, and the workspace is sized once for
+``world * cap`` rows. The pushes run on a side stream on ``2 * push_sms``
+CTAs while the shared expert's GEMMs leave ``push_sms`` SMs free.
 """
 from __future__ import annotations
 
@@ -220,6 +224,8 @@ class EPLayer:
         self._flag = None
         self.overlap = True  # CUDA tensors: exchange on a side stream, shared expert while rows travel
         self.sm_reserve = 0  # SMs left to the collectives while GEMMs and all-to-alls overlap
+        self.push_sms = 16  # peer-memory step: SMs the shared expert leaves to the row pushes (0 = no overlap)
+        self._push_status = None
 
     # -------------------------------------------------------------- phases
     def route(self, x: torch.Tensor):
@@ -312,12 +318,35 @@ class EPLayer:
             self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
         self.exchange.dist.all_reduce(self._flag, group=self.exchange.group)
 
+    def _peer_workspace(self, dev):
+        """Workspace of the peer-memory step, sized once for the most rows a
+        rank can receive (world * cap), so that the step never needs the
+        received-row count on the host."""
+        pb = self.peer
+        need = lib().dsmoe_moe_local_workspace_size(_lib.moe_config(self.lcfg), self.world * pb.cap)
+        if self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        if self._push_status is None:
+            self._push_status = torch.zeros(1, dtype=torch.int32, device=dev)
+        return self._ws
+
+    def push_status(self) -> int:
+        """The push kernel's device error word (read and cleared; a host sync:
+        diagnostics only). Non-zero: gathered counts that did not fit the
+        receive buffers."""
+        if self._push_status is None:
+            return 0
+        v = int(self._push_status.item())
+        self._push_status.zero_()
+        return v
+
     def _forward_peer(self, x: torch.Tensor) -> torch.Tensor:
         cfg, pb = self.config, self.peer
         T, H = x.shape
         K, W, dev = cfg.num_experts_per_tok, self.world, x.device
         if T > pb.cap:
             raise ValueError(f"{T} tokens exceed the peer buffers' capacity of {pb.cap}")
+        ws = self._peer_workspace(dev)
         idx, w = self.route(x)
         counts = torch.empty(W, dtype=torch.int32, device=dev)
         tok_rows = torch.empty(T, W, dtype=torch.int32, device=dev)
@@ -325,31 +354,53 @@ class EPLayer:
         send_tok = torch.empty(n_send, dtype=torch.int32, device=dev)
         send_idx = torch.empty(n_send, K, dtype=torch.int32, device=dev)
         send_w = torch.empty(n_send, K, dtype=torch.float32, device=dev)
-        stream = stream_handle(dev)
+        cs = torch.cuda.current_stream(dev)
         check(lib().dsmoe_ep_plan(ptr(idx), ptr(w), T, K, W, self.El, ptr(counts), ptr(tok_rows), ptr(send_tok),
-                                  ptr(send_idx), ptr(send_w), stream), "dsmoe_ep_plan")
+                                  ptr(send_idx), ptr(send_w), stream_handle(dev)), "dsmoe_ep_plan")
         counts_all = torch.empty(W * W, dtype=torch.int32, device=dev)  # row s: what rank s sends to each rank
         self.exchange.dist.all_gather_into_tensor(counts_all, counts, group=self.exchange.group)
-        rows = int(counts_all.view(W, W)[:, self.rank].sum().item())  # rows this rank receives
+        overlap = self.overlap and self.push_sms > 0
+        push_stream = cs
+        if overlap:
+            # The pushes travel over NVLink on a side stream, on a capped grid,
+            # while the shared expert (which needs no exchange) computes on the
+            # SMs its GEMMs leave free of them.
+            if self._comm is None:
+                self._comm = torch.cuda.Stream(device=dev)
+            push_stream = self._comm
+            ready = torch.cuda.Event()
+            ready.record(cs)
+            push_stream.wait_event(ready)
+            for t_ in (x, counts_all, send_tok, send_idx, send_w, tok_rows):
+                t_.record_stream(push_stream)
         check(lib().dsmoe_ep_push(ptr(x), T, K, H, W, self.rank, pb.cap, ptr(counts_all), ptr(send_tok),
                                   ptr(send_idx), ptr(send_w), ptr(tok_rows), ptr(pb.tables["x"]),
-                                  ptr(pb.tables["meta"]), stream), "dsmoe_ep_push")
-        shared = self.shared_ffn(x)  # independent of the exchange
+                                  ptr(pb.tables["meta"]), ptr(self._push_status),
+                                  2 * self.push_sms if overlap else 0, push_stream.cuda_stream), "dsmoe_ep_push")
+        if overlap:
+            n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+            try:
+                _lib.set_gemm_sm_limit(max(1, n_sm - self.push_sms))
+                shared = self.shared_ffn(x)
+            finally:
+                _lib.set_gemm_sm_limit(0)
+            pushed = torch.cuda.Event()
+            pushed.record(push_stream)
+            cs.wait_event(pushed)
+        else:
+            shared = self.shared_ffn(x)
         self._barrier(dev)  # every rank's rows have landed
-        if rows:
-            lcfg = _lib.moe_config(self.lcfg)
-            need = lib().dsmoe_moe_local_workspace_size(lcfg, rows)
-            if self._ws.numel() < need:
-                self._ws = torch.zeros(int(need * 1.25) + 4096, dtype=torch.uint8, device=dev)
-            b = self.bank
-            lw = _lib.LayerWeights(
-                gate_weight=None, score_bias=None, n_slots=b.n_slots,
-                w_gate=ptr(b.w["gate_proj"]), s_gate=ptr(b.s["gate_proj"]), w_up=ptr(b.w["up_proj"]),
-                s_up=ptr(b.s["up_proj"]), w_down=ptr(b.w["down_proj"]), s_down=ptr(b.s["down_proj"]),
-                slot_of_expert=ptr(b.slot_of))
-            check(lib().dsmoe_moe_local_peer(lcfg, lw, pb.own["x"], rows, pb.own["meta"], W, self.rank, pb.cap,
-                                             ptr(pb.tables["back"]), ptr(self._ws), self._ws.numel(), stream),
-                  "dsmoe_moe_local_peer")
+        lcfg = _lib.moe_config(self.lcfg)
+        b = self.bank
+        lw = _lib.LayerWeights(
+            gate_weight=None, score_bias=None, n_slots=b.n_slots,
+            w_gate=ptr(b.w["gate_proj"]), s_gate=ptr(b.s["gate_proj"]), w_up=ptr(b.w["up_proj"]),
+            s_up=ptr(b.s["up_proj"]), w_down=ptr(b.w["down_proj"]), s_down=ptr(b.s["down_proj"]),
+            slot_of_expert=ptr(b.slot_of))
+        # rows received are counted on the device from counts_all; W * cap bounds them
+        check(lib().dsmoe_moe_local_peer(lcfg, lw, pb.own["x"], W * pb.cap, pb.own["meta"], W, self.rank, pb.cap,
+                                         ptr(pb.tables["back"]), ptr(counts_all), ptr(ws), ws.numel(),
+                                         stream_handle(dev)), "dsmoe_moe_local_peer")
         self._barrier(dev)  # every partial is back at its origin
         back = pb.views["back"].view(torch.bfloat16).view(W * pb.cap, H)
         return self.combine(shared, back, tok_rows)

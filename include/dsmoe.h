@@ -251,7 +251,9 @@ DSMOE_API int dsmoe_ep_combine(const void* partials, const int32_t* tok_rows, in
  *      sum_{s < rank} counts_all[s][d] + k, with its local expert ids,
  *      weights and origin (rank, k); rewrites tok_rows[t][d] to d * cap + k.
  *   4. a barrier across ranks (the caller's), then on every rank
- *      dsmoe_moe_local_peer over its rows received (sum of counts_all[.][rank]):
+ *      dsmoe_moe_local_peer over its rows received (sum of counts_all[.][rank];
+ *      given counts_all, the library counts them on the device and `rows` is
+ *      only a bound, e.g. world * cap, so the host never reads the counts):
  *      the grouped GEMMs of dsmoe_moe_local, whose combine writes each partial
  *      row into the ORIGIN rank's return buffer (peer_return[s]) at row
  *      rank * cap + k.
@@ -266,11 +268,17 @@ DSMOE_API int dsmoe_ep_plan(const int64_t* topk_idx, const float* topk_w, int32_
 DSMOE_API int dsmoe_ep_push(const void* hidden, int32_t tokens, int32_t top_k, int32_t hidden_size, int32_t world,
                             int32_t rank, int32_t cap, const int32_t* counts_all, const int32_t* send_tok,
                             const int32_t* send_idx, const float* send_w, int32_t* tok_rows,
-                            const uint64_t* peer_recv_hidden, const uint64_t* peer_recv_meta, dsmoe_stream_t stream);
+                            const uint64_t* peer_recv_hidden, const uint64_t* peer_recv_meta, int32_t* device_status,
+                            int32_t max_blocks, dsmoe_stream_t stream);
+/* device_status (may be NULL): error word set (code 6) when the gathered
+ * counts do not fit the receive buffers; such rows are not written and their
+ * tok_rows entry becomes -1. max_blocks > 0 caps the push's grid, so that it
+ * can run beside a grouped GEMM whose grid leaves that many SMs free
+ * (dsmoe_set_gemm_sm_limit). */
 DSMOE_API int dsmoe_moe_local_peer(const dsmoe_moe_config_t* cfg, const dsmoe_layer_weights_t* weights,
                                    const void* recv_hidden, int32_t rows, const int32_t* recv_meta, int32_t world,
-                                   int32_t rank, int32_t cap, const uint64_t* peer_return, void* workspace,
-                                   size_t workspace_bytes, dsmoe_stream_t stream);
+                                   int32_t rank, int32_t cap, const uint64_t* peer_return, const int32_t* counts_all,
+                                   void* workspace, size_t workspace_bytes, dsmoe_stream_t stream);
 DSMOE_API size_t dsmoe_ep_meta_bytes(int32_t world, int32_t cap, int32_t top_k);
 
 /*

@@ -105,8 +105,9 @@ def test_ep_overlapped_two_stream_step(chunks, reserve):
 def test_ep_peer_memory_one_rank_group():
     """The peer-memory exchange (rows pushed into mapped receive buffers,
     partials written back into the origin's return buffer, tiny NCCL
-    barriers) on a one-rank NCCL group gives the all-to-all step's output
-    bit for bit."""
+    barriers, received rows counted on the device) on a one-rank NCCL group
+    gives the all-to-all step's output bit for bit, with the pushes
+    overlapping the shared expert or not."""
     import socket
 
     import torch.distributed as dist
@@ -127,10 +128,13 @@ def test_ep_peer_memory_one_rank_group():
         plain = [layer.forward(x) for x in xs]
         layer.use_peer_memory(cap=128)
         try:
-            peer = [layer.forward(x) for x in xs]
-            torch.cuda.synchronize()
-            for a, b in zip(plain, peer):
-                assert torch.equal(a, b)
+            for push_sms in (16, 0):  # pushes beside the shared expert on a side stream, then in order
+                layer.push_sms = push_sms
+                peer = [layer.forward(x) for x in xs]
+                torch.cuda.synchronize()
+                for a, b in zip(plain, peer):
+                    assert torch.equal(a, b)
+                assert layer.push_status() == 0
             with pytest.raises(ValueError):
                 layer.forward(activations(90, 129, H).to(DEV))
         finally:
