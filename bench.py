@@ -417,10 +417,16 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
+    default_run = args.config is None
     if args.config is None:
         args.config = 2 if world == 1 else 3
     if args.tokens is None:
-        args.tokens = {2: 4096, 3: 8192, 4: 16384, 5: 1}[args.config]
+        # The default N > 1 run keeps the N = 1 line's per-GPU batch (4096
+        # tokens) so that the 1 -> N curve compares equal per-GPU work (weak
+        # scaling); config 3's own 8192 tokens per GPU is measured in the same
+        # run (config3_t8192) and is the default of an explicit --config 3.
+        args.tokens = {2: 4096, 3: 4096 if default_run else 8192, 4: 16384, 5: 1}[args.config]
+    args.extra_config3 = default_run and world > 1 and args.mode == "ep" and args.tokens != 8192
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
@@ -434,6 +440,7 @@ def main():
 
     from dsmoe import DeepSeekConfig, GPUTransfer, SyntheticWeightStore, moe_block
     from dsmoe._lib import Workspace, set_profile_events
+    from dsmoe.ep import PEER_PHASES
     from dsmoe.synthetic import activations
 
     torch.cuda.set_device(local)
@@ -460,7 +467,7 @@ def main():
         ep_layer.sm_reserve = args.sm_reserve
         ep_layer.overlap = not args.no_overlap
         if not args.nccl_exchange:
-            ep_layer.use_peer_memory(cap=T)
+            ep_layer.use_peer_memory(cap=max(T, 8192 if args.extra_config3 else 0))
         bank = None
         x = activations(1000 * seed + rank, T, H, device=dev)
 
@@ -483,9 +490,11 @@ def main():
     # themselves. The expert-parallel step is timed whole; its phases are
     # measured in a separate pass below.
     names = ["router", "permute", "gate_up", "swiglu_quant", "down", "combine"]
-    evsets = None if ep else [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
-                              for _ in range(args.steps)]
-    for evs in evsets or []:
+    evsets = [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)] for _ in range(args.steps)]
+    # expert-parallel peer-memory step: its phases on the compute stream
+    phsets = ([[torch.cuda.Event(enable_timing=True) for _ in range(len(PEER_PHASES) + 1)]
+               for _ in range(args.steps)] if ep and not args.nccl_exchange else None)
+    for evs in evsets + (phsets or []):
         for e in evs:
             e.record()  # create the CUDA events before the timed region
     for _ in range(args.warmup):
@@ -502,13 +511,18 @@ def main():
     t_begin = time.time()
     e0.record()
     for i in range(args.steps):
-        if evsets:
+        if ep:  # the library's events around the rank's expert GEMMs only
+            ep_layer.lib_events = evsets[i]
+            ep_layer.phase_events = phsets[i] if phsets else None
+        else:
             set_profile_events(evsets[i])
         step(x)
     e1.record()
     torch.cuda.synchronize()
     t_end = time.time()
-    if evsets:
+    if ep:
+        ep_layer.lib_events = ep_layer.phase_events = None
+    else:
         set_profile_events(None)
     if world > 1:
         dist.barrier()
@@ -522,63 +536,51 @@ def main():
 
     # ------------------------------------------------- per-stage (roofline)
     stage_ms = [0.0] * len(names)
-    if evsets:
-        for evs in evsets:
-            for i in range(len(names)):
-                stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / len(evsets)
+    first = 2 if ep else 0  # expert-parallel: the library events cover the rank's expert GEMMs (stages 2..5)
+    for evs in evsets:
+        for i in range(first, len(names)):
+            stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / len(evsets)
+    ep_phases = None
+    if phsets:
+        ep_phases = {nm: sum(ev[i].elapsed_time(ev[i + 1]) for ev in phsets) / len(phsets)
+                     for i, nm in enumerate(PEER_PHASES)}
+        ep_phases["decomposition"] = ("peer-memory step, phase by phase on the compute stream inside the timed "
+                                      "steps (the pushes run on a side stream beside the shared expert)")
+    if not ep:
         out, idx, _w = moe_block(x, LAYER, store, gt, cfg, return_routing=True)  # the (deterministic) routing
     else:
-        # the rank's expert GEMMs phase by phase (events recorded by the
-        # library at its stage boundaries), after the timed region
-        names[1] = "dispatch+all_to_all+permute"
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
-        n_prof = min(20, max(3, args.steps // 2))
-        for _ in range(n_prof):
-            set_profile_events(evs)
+        names[0] = names[1] = None  # not timed separately on the expert-parallel path
+        # what this rank's GEMMs processed: its local (row, expert) pairs
+        if args.nccl_exchange:
             counts_d, tok_rows, send_x, meta = ep_layer.dispatch(x)
             sc, rc = ep_layer.exchange.counts(counts_d)
-            recv_meta = ep_layer.exchange.rows(meta, sc, rc)
-            part = ep_layer.compute(ep_layer.exchange.rows(send_x, sc, rc), recv_meta)
-            set_profile_events(None)  # the shared-expert FFN must not re-record them
-            ep_layer.finish(x, ep_layer.exchange.rows(part, rc, sc), tok_rows)
-            torch.cuda.synchronize()
-            for i in range(len(names)):
-                stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / n_prof
-    ep_phases = None
-    if ep:
-        # the one-chunk step phase by phase, events on the compute stream
-        # (NCCL calls make it wait for their completion)
-        pnames = ["route", "pack", "count_exchange_host_sync", "rows_all_to_all", "expert_gemms",
-                  "partials_all_to_all", "shared_expert", "combine"]
-        pev = [torch.cuda.Event(enable_timing=True) for _ in range(len(pnames) + 1)]
-        ep_phases = dict.fromkeys(pnames, 0.0)
-        for it in range(n_prof + 1):  # the first pass is untimed: it sets up the all-to-all path's buffers
-            pev[0].record()
-            idx_, w_ = ep_layer.route(x)
-            pev[1].record()
-            counts_d, tok_rows, send_x, meta = ep_layer.pack(x, idx_, w_)
-            pev[2].record()
-            sc, rc = ep_layer.exchange.counts(counts_d)
-            pev[3].record()
-            recv_meta = ep_layer.exchange.rows(meta, sc, rc)
-            recv_x = ep_layer.exchange.rows(send_x, sc, rc)
-            pev[4].record()
-            part = ep_layer.compute(recv_x, recv_meta)
-            pev[5].record()
-            back = ep_layer.exchange.rows(part, rc, sc)
-            pev[6].record()
-            shared = ep_layer.shared_ffn(x)
-            pev[7].record()
-            ep_layer.combine(shared, back, tok_rows)
-            pev[8].record()
-            torch.cuda.synchronize()
-            if it == 0:
-                continue
-            for i, nme in enumerate(pnames):
-                ep_phases[nme] += pev[i].elapsed_time(pev[i + 1]) / n_prof
-        ep_phases["decomposition"] = "all-to-all step, phase by phase on the compute stream"
-        ep_phases["rows_per_rank_received"] = int(recv_x.shape[0])
-        ep_phases["rows_per_rank_sent"] = int(sum(sc))
+            lidx = ep_layer.exchange.rows(meta, sc, rc)[:, :TOPK].reshape(-1)
+        else:
+            step(x)
+            rows_recv, _ = ep_layer.received_pairs()
+            pbm = ep_layer.peer.views["meta"].view(torch.int32)
+            lidx = pbm[: world * ep_layer.peer.cap * TOPK].view(-1, TOPK)[:rows_recv].reshape(-1)
+            ep_phases["rows_per_rank_received"] = rows_recv
+        lidx = lidx[lidx >= 0].long()
+    config3 = None
+    if args.extra_config3:
+        # config 3's own shape (8192 tokens per GPU), same layer and exchange
+        x8 = activations(1000 * seed + rank, 8192, H, device=dev)
+        for _ in range(3):
+            step(x8)
+        torch.cuda.synchronize()
+        dist.barrier()
+        a8, b8 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a8.record()
+        for _ in range(10):
+            step(x8)
+        b8.record()
+        torch.cuda.synchronize()
+        ms8 = torch.tensor([a8.elapsed_time(b8) / 10], device=dev)
+        dist.all_reduce(ms8, op=dist.ReduceOp.MAX)
+        config3 = {"tokens_per_gpu": 8192, "value": world * 8192 / (float(ms8.item()) / 1e3),
+                   "ms_per_step": float(ms8.item()), "steps": 10, "unit": UNIT}
+        del x8
     from dsmoe.ops import route as _route
     _gidx, _ = _route(x, store.get_gate_weight(LAYER), cfg,
                       score_bias=store.get_gate_bias(LAYER) if skew else None)
@@ -586,8 +588,6 @@ def main():
     hottest_over_mean = float(gcounts.max() / gcounts.mean())
     if ep:
         # the rank's own GEMM work: its experts over the rows it received (no shared expert there)
-        lidx = recv_meta[:, :TOPK].reshape(-1)
-        lidx = lidx[lidx >= 0].long()
         counts = torch.bincount(lidx, minlength=ep_layer.El).cpu()
         touched = int((counts > 0).sum())
         rows = int(lidx.numel())
@@ -628,8 +628,7 @@ def main():
     roofline["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch on this "
                                   "workload (profiles/)" if traffic else None)
     roofline["timing"] = ("mean of the launch's CUDA-event duration over the timed steps (events recorded by the "
-                          "library at its stage boundaries on the launching stream)" if not ep else
-                          "separate profiling pass after the timed region")
+                          "library at its stage boundaries on the launching stream)")
     layer_bytes = gateup_bytes + swiglu_bytes + down_bytes
     layer_ms = sum(stage_ms)
 
@@ -804,8 +803,9 @@ def main():
                     "copies": "pinned host buffers; H2D and D2H on their own streams, double-buffered, "
                               "overlapping the neighbouring steps' compute"},
             "roofline": roofline,
-            "stages_ms": dict(zip(names, stage_ms)),
-            "stages_sum_over_step": sum(stage_ms) / ms_max,
+            "stages_ms": {nm: v for nm, v in zip(names, stage_ms) if nm},
+            "stages_sum_over_step": None if ep else sum(stage_ms) / ms_max,
+            **({"config3_t8192": config3} if config3 else {}),
             **({"ep_phases_ms": ep_phases} if ep_phases else {}),
             "layer": {"algorithmic_bytes": layer_bytes, "GB_s": layer_bytes / (layer_ms / 1e3) / 1e9,
                       "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm_peak,
@@ -816,8 +816,10 @@ def main():
             **({"decode_rows": decode} if decode else {}),
             **({"streaming_config5": streaming} if streaming else {}),
             # library kernels per step: router 2, count/plan/scatter 3, GEMMs 2, swiglu 1, combine 1;
-            # expert-parallel: + dispatch 3, + shared-expert FFN 5 (its own plan/scatter/GEMMs/swiglu)
-            "gpu_launches": (18 if ep else 9) * args.steps,
+            # expert-parallel over peer memory: router 2, plan 2, push 1, shared-expert FFN 5 (plan,
+            # scatter, 2 GEMMs, swiglu), received-row count 1, the rank's experts 7 (count, plan, scatter,
+            # 2 GEMMs, swiglu, combine-and-return), final combine 1
+            "gpu_launches": (19 if ep else 9) * args.steps,
             "device_status": status,
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -196,6 +196,10 @@ def local_config(config, world: int):
     return config.with_(n_routed_experts=El, n_group=ng, topk_group=ng)
 
 
+PEER_PHASES = ("route_plan_count_gather", "push_beside_shared_expert", "barrier_rows_landed",
+               "expert_gemms_partials_return", "barrier_partials_back", "combine")
+
+
 class EPLayer:
     """One MoE layer, expert-parallel. ``expert_source(layer, e)`` returns expert
     ``e``'s ``{proj: (weight, scale)}`` (any device); by default the weight
@@ -226,6 +230,12 @@ class EPLayer:
         self.sm_reserve = 0  # SMs left to the collectives while GEMMs and all-to-alls overlap
         self.push_sms = 16  # peer-memory step: SMs the shared expert leaves to the row pushes (0 = no overlap)
         self._push_status = None
+        # Optional timing of the peer-memory step (CUDA events recorded on the
+        # compute stream): phase_events[0..6] at the PEER_PHASES boundaries,
+        # lib_events (7) handed to the library around the rank's expert GEMMs.
+        self.phase_events = None
+        self.lib_events = None
+        self.last_counts_all = None
 
     # -------------------------------------------------------------- phases
     def route(self, x: torch.Tensor):
@@ -279,8 +289,14 @@ class EPLayer:
             w_gate=ptr(b.w["gate_proj"]), s_gate=ptr(b.s["gate_proj"]), w_up=ptr(b.w["up_proj"]),
             s_up=ptr(b.s["up_proj"]), w_down=ptr(b.w["down_proj"]), s_down=ptr(b.s["down_proj"]),
             slot_of_expert=ptr(b.slot_of))
-        check(lib().dsmoe_moe_local(cfg, lw_struct, ptr(recv_x), R, ptr(lidx), ptr(lw), ptr(out), ptr(self._ws),
-                                    self._ws.numel(), stream_handle(recv_x.device)), "dsmoe_moe_local")
+        if self.lib_events:
+            _lib.set_profile_events(self.lib_events)
+        try:
+            check(lib().dsmoe_moe_local(cfg, lw_struct, ptr(recv_x), R, ptr(lidx), ptr(lw), ptr(out), ptr(self._ws),
+                                        self._ws.numel(), stream_handle(recv_x.device)), "dsmoe_moe_local")
+        finally:
+            if self.lib_events:
+                _lib.set_profile_events(None)
         return out
 
     def shared_ffn(self, x: torch.Tensor) -> torch.Tensor:
@@ -347,6 +363,10 @@ class EPLayer:
         if T > pb.cap:
             raise ValueError(f"{T} tokens exceed the peer buffers' capacity of {pb.cap}")
         ws = self._peer_workspace(dev)
+        ev = self.phase_events
+        cs = torch.cuda.current_stream(dev)
+        if ev:
+            ev[0].record(cs)
         idx, w = self.route(x)
         counts = torch.empty(W, dtype=torch.int32, device=dev)
         tok_rows = torch.empty(T, W, dtype=torch.int32, device=dev)
@@ -354,11 +374,13 @@ class EPLayer:
         send_tok = torch.empty(n_send, dtype=torch.int32, device=dev)
         send_idx = torch.empty(n_send, K, dtype=torch.int32, device=dev)
         send_w = torch.empty(n_send, K, dtype=torch.float32, device=dev)
-        cs = torch.cuda.current_stream(dev)
         check(lib().dsmoe_ep_plan(ptr(idx), ptr(w), T, K, W, self.El, ptr(counts), ptr(tok_rows), ptr(send_tok),
                                   ptr(send_idx), ptr(send_w), stream_handle(dev)), "dsmoe_ep_plan")
         counts_all = torch.empty(W * W, dtype=torch.int32, device=dev)  # row s: what rank s sends to each rank
         self.exchange.dist.all_gather_into_tensor(counts_all, counts, group=self.exchange.group)
+        self.last_counts_all = counts_all
+        if ev:
+            ev[1].record(cs)
         overlap = self.overlap and self.push_sms > 0
         push_stream = cs
         if overlap:
@@ -389,7 +411,11 @@ class EPLayer:
             cs.wait_event(pushed)
         else:
             shared = self.shared_ffn(x)
+        if ev:
+            ev[2].record(cs)
         self._barrier(dev)  # every rank's rows have landed
+        if ev:
+            ev[3].record(cs)
         lcfg = _lib.moe_config(self.lcfg)
         b = self.bank
         lw = _lib.LayerWeights(
@@ -398,12 +424,33 @@ class EPLayer:
             s_up=ptr(b.s["up_proj"]), w_down=ptr(b.w["down_proj"]), s_down=ptr(b.s["down_proj"]),
             slot_of_expert=ptr(b.slot_of))
         # rows received are counted on the device from counts_all; W * cap bounds them
-        check(lib().dsmoe_moe_local_peer(lcfg, lw, pb.own["x"], W * pb.cap, pb.own["meta"], W, self.rank, pb.cap,
-                                         ptr(pb.tables["back"]), ptr(counts_all), ptr(ws), ws.numel(),
-                                         stream_handle(dev)), "dsmoe_moe_local_peer")
+        if self.lib_events:
+            _lib.set_profile_events(self.lib_events)
+        try:
+            check(lib().dsmoe_moe_local_peer(lcfg, lw, pb.own["x"], W * pb.cap, pb.own["meta"], W, self.rank,
+                                             pb.cap, ptr(pb.tables["back"]), ptr(counts_all), ptr(ws), ws.numel(),
+                                             stream_handle(dev)), "dsmoe_moe_local_peer")
+        finally:
+            if self.lib_events:
+                _lib.set_profile_events(None)
+        if ev:
+            ev[4].record(cs)
         self._barrier(dev)  # every partial is back at its origin
+        if ev:
+            ev[5].record(cs)
         back = pb.views["back"].view(torch.bfloat16).view(W * pb.cap, H)
-        return self.combine(shared, back, tok_rows)
+        out = self.combine(shared, back, tok_rows)
+        if ev:
+            ev[6].record(cs)
+        return out
+
+    def received_pairs(self) -> tuple[int, int]:
+        """(rows, (row, local expert) pairs) this rank received in the last
+        peer-memory step (a host read: diagnostics only)."""
+        W, K = self.world, self.config.num_experts_per_tok
+        rows = int(self.last_counts_all.view(W, W)[:, self.rank].sum().item())
+        meta = self.peer.views["meta"].view(torch.int32)[: W * self.peer.cap * K].view(W * self.peer.cap, K)
+        return rows, int((meta[:rows] >= 0).sum().item())
 
     def forward(self, x: torch.Tensor, chunks: int = 1) -> torch.Tensor:
         """One expert-parallel MoE step for this rank's tokens ``x`` [T, H] bf16.
