@@ -26,7 +26,7 @@ EXPORTED = (
     "dsmoe_ep_combine", "dsmoe_set_gemm_sm_limit", "dsmoe_rms_norm", "dsmoe_moe_layer_ffn_workspace_size",
     "dsmoe_moe_layer_ffn", "dsmoe_read_ranges", "dsmoe_ep_plan", "dsmoe_ep_push", "dsmoe_moe_local_peer",
     "dsmoe_ep_meta_bytes", "dsmoe_ipc_alloc", "dsmoe_ipc_open", "dsmoe_ipc_close", "dsmoe_ipc_free",
-    "dsmoe_sample_top_p",
+    "dsmoe_sample_top_p", "dsmoe_slotcache_state_bytes", "dsmoe_slotcache_step", "dsmoe_map_host_pointers",
 )
 
 
@@ -46,6 +46,18 @@ class LayerWeights(ctypes.Structure):
         ("w_up", ctypes.c_void_p), ("s_up", ctypes.c_void_p),
         ("w_down", ctypes.c_void_p), ("s_down", ctypes.c_void_p),
         ("slot_of_expert", ctypes.c_void_p),
+    ]
+
+
+class SlotCacheDesc(ctypes.Structure):
+    """``dsmoe_slotcache_t`` (include/dsmoe.h)."""
+    _fields_ = [
+        ("n_experts", ctypes.c_int32), ("n_slots", ctypes.c_int32), ("hidden", ctypes.c_int32),
+        ("inter", ctypes.c_int32),
+        ("w_gate", ctypes.c_void_p), ("s_gate", ctypes.c_void_p), ("w_up", ctypes.c_void_p),
+        ("s_up", ctypes.c_void_p), ("w_down", ctypes.c_void_p), ("s_down", ctypes.c_void_p),
+        ("slot_of", ctypes.c_void_p), ("state", ctypes.c_void_p), ("host_src", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
     ]
 
 
@@ -102,6 +114,10 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_sample_top_p.argtypes = [vp, i32, i32, ctypes.c_int64, ctypes.c_float, ctypes.c_float, vp, vp,
                                                  vp, vp]
                 u64p = ctypes.POINTER(ctypes.c_uint64)
+                L.dsmoe_slotcache_state_bytes.argtypes = [i32]
+                L.dsmoe_slotcache_state_bytes.restype = sz
+                L.dsmoe_slotcache_step.argtypes = [ctypes.POINTER(SlotCacheDesc), vp, i32, vp]
+                L.dsmoe_map_host_pointers.argtypes = [u64p, i32, u64p]
                 L.dsmoe_read_ranges.argtypes = [i32, ctypes.POINTER(ctypes.c_char_p), u64p, u64p,
                                                 ctypes.POINTER(vp), i32]
                 for name in EXPORTED:

@@ -10,7 +10,9 @@ one sequence of CUDA kernels on the current stream:
   -> grouped down GEMM -> weighted combine with the shared expert.
 
 ``gpu_transfer`` must be this package's ``GPUTransfer``: it owns the layer's
-device weight bank. In streaming mode (fewer slots than experts) the routing is
+device weight bank. In streaming mode (fewer slots than experts) with a
+device-managed slot table (``device_slots``) the missing experts are placed
+and copied by ``dsmoe_slotcache_step`` on the device; otherwise the routing is
 read back once per block (the reference reads it back once per token, via
 ``.tolist()``) to bring missing experts in before the expert GEMMs.
 """
@@ -62,10 +64,14 @@ def moe_block(hidden: torch.Tensor, layer_idx: int, weight_store, gpu_transfer, 
     else:
         check(lib().dsmoe_route(cfg, ptr(x), ptr(gate_weight), ptr(bias), T, ptr(idx), ptr(w), ptr(ws), ws.numel(),
                                 stream), "dsmoe_route")
-        experts = torch.unique(idx).tolist()  # one device->host read per block
-        if verbose:
-            print(f"      [moe L{layer_idx:02d}] {T} tokens -> {len(experts)} distinct experts")
-        bank = gpu_transfer.ensure_resident(layer_idx, experts)
+        dc = gpu_transfer.device_cache(layer_idx)
+        if dc is not None:
+            dc.step(idx)  # slot table and copies on the device: no host read
+        else:
+            experts = torch.unique(idx).tolist()  # one device->host read per block
+            if verbose:
+                print(f"      [moe L{layer_idx:02d}] {T} tokens -> {len(experts)} distinct experts")
+            bank = gpu_transfer.ensure_resident(layer_idx, experts)
         lw = _layer_weights(bank, gate_weight, bias)
         check(lib().dsmoe_moe_experts(cfg, lw, ptr(x), T, ptr(out), ptr(ws), ws.numel(), stream),
               "dsmoe_moe_experts")

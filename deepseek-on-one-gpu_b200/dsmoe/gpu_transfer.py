@@ -16,14 +16,26 @@ device-side ``slot_of`` table (group -> slot) that the grouped GEMMs read.
 
 ``transfer_experts`` keeps the reference signature and return value (a list
 of ``{proj: (weight, scale)}`` per requested expert, views into the bank).
+
+Device-managed streaming (``device_slots=True``, when the weight store holds
+every routed expert of a layer in pinned host memory): the slot table is kept
+on the GPU by ``dsmoe_slotcache_step`` (``DeviceSlotCache``), which places the
+step's missing experts in least-recently-used slots and copies them from host
+memory with the SMs, all on the compute stream: the routing is never read
+back and the host never waits.
 """
 from __future__ import annotations
 
+import ctypes
 from collections import OrderedDict
 
 import torch
 
+from . import _lib
+from ._lib import check, lib, ptr, stream_handle
 from .synthetic import PROJS
+
+PINNED_SLOT = 0x7FFFFFFF  # last_use of the shared expert's slot: never taken
 
 
 class LayerBank:
@@ -101,11 +113,67 @@ class LayerBank:
         return {p: (self.w[p][s], self.s[p][s]) for p in PROJS}
 
 
+class DeviceSlotCache:
+    """The slot table of one ``LayerBank`` kept on the device
+    (``dsmoe_slotcache_step``): each step marks the experts its routing needs,
+    refreshes their recency, gives every missing expert the least recently
+    used slot the step does not need and copies it in from pinned host memory.
+    After construction the bank's host-side mirrors are no longer maintained;
+    ``refresh_host_mirror`` reads the device table back (a host sync, for
+    inspection only)."""
+
+    def __init__(self, bank: LayerBank, config, host_ptrs: list[int]):
+        E, H, F = config.n_routed_experts, config.hidden_size, config.moe_intermediate_size
+        if len(host_ptrs) != 6 * E:
+            raise ValueError("need 6 host tensors per routed expert")
+        self.bank, self.device = bank, bank.device
+        src = (ctypes.c_uint64 * (6 * E))(*host_ptrs)
+        dev = (ctypes.c_uint64 * (6 * E))()
+        check(lib().dsmoe_map_host_pointers(src, 6 * E, dev), "dsmoe_map_host_pointers")
+        self.src = torch.tensor([int(v) for v in dev], dtype=torch.int64).to(self.device)  # uint64 bits
+        n = bank.n_slots
+        st = torch.zeros(lib().dsmoe_slotcache_state_bytes(n) // 4, dtype=torch.int32)
+        st[4:4 + n] = torch.tensor(bank.group_in_slot, dtype=torch.int32)
+        last = [-1 if g < 0 else (PINNED_SLOT if g == 0 else 0) for g in bank.group_in_slot]
+        st[4 + n:4 + 2 * n] = torch.tensor(last, dtype=torch.int32)
+        bank.sync_table(non_blocking=False)
+        self.state = st.to(self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.desc = _lib.SlotCacheDesc(
+            n_experts=E, n_slots=n, hidden=H, inter=F,
+            w_gate=ptr(bank.w["gate_proj"]), s_gate=ptr(bank.s["gate_proj"]), w_up=ptr(bank.w["up_proj"]),
+            s_up=ptr(bank.s["up_proj"]), w_down=ptr(bank.w["down_proj"]), s_down=ptr(bank.s["down_proj"]),
+            slot_of=ptr(bank.slot_of), state=ptr(self.state), host_src=ptr(self.src), status=ptr(self.status))
+        bank.device_managed = True
+
+    def step(self, topk_idx: torch.Tensor) -> None:
+        """Make the experts of ``topk_idx`` (int64, any shape) resident, on
+        the current stream."""
+        idx = topk_idx.contiguous()
+        check(lib().dsmoe_slotcache_step(ctypes.byref(self.desc), ptr(idx), idx.numel(),
+                                         stream_handle(self.device)), "dsmoe_slotcache_step")
+
+    def counters(self) -> tuple[int, int]:
+        """(hits, misses) so far (a host read)."""
+        v = self.state[2:4].tolist()
+        return int(v[0]), int(v[1])
+
+    def device_status(self) -> int:
+        return int(self.status.item())
+
+    def refresh_host_mirror(self) -> None:
+        b = self.bank
+        b.slot_of_host = b.slot_of.tolist()
+        n = b.n_slots
+        b.group_in_slot = self.state[4:4 + n].tolist()
+
+
 class GPUTransfer:
     """Expert residency manager with the reference's constructor and
     ``transfer_experts`` signature (``inference/gpu_transfer.py:15-16,50-52``)."""
 
-    def __init__(self, config, weight_store, device, verbose: bool = False, slots_per_layer: int | None = None):
+    def __init__(self, config, weight_store, device, verbose: bool = False, slots_per_layer: int | None = None,
+                 device_slots: bool = False):
         self.config = config
         self.weight_store = weight_store
         self.device = torch.device(device)
@@ -119,6 +187,8 @@ class GPUTransfer:
         self.slot_hits = 0
         self.slot_misses = 0
         self.prefetched = 0
+        self.device_slots = device_slots
+        self.dcache: dict[int, DeviceSlotCache] = {}
 
     @property
     def resident(self) -> bool:
@@ -139,6 +209,19 @@ class GPUTransfer:
             b.sync_table(non_blocking=False)
             torch.cuda.current_stream(self.device).synchronize()
         return b
+
+    def device_cache(self, layer: int) -> DeviceSlotCache | None:
+        """The layer's device-managed slot table (streaming mode with
+        ``device_slots`` and every routed expert in pinned host memory)."""
+        if self.resident or not self.device_slots:
+            return None
+        dc = self.dcache.get(layer)
+        if dc is None:
+            ptrs = getattr(self.weight_store, "host_expert_pointers", lambda _l: None)(layer)
+            if ptrs is None:
+                return None
+            dc = self.dcache[layer] = DeviceSlotCache(self.bank(layer), self.config, ptrs)
+        return dc
 
     def prefetch(self, layer: int, experts) -> int:
         """Start bringing `experts` (routed ids) into the layer's bank on the side

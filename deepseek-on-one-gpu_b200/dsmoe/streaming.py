@@ -32,13 +32,15 @@ from .gpu_transfer import GPUTransfer
 
 
 class StreamingDecoder:
-    def __init__(self, config, weight_store, device, layers, slots_per_layer: int = 65, prefetch: bool = True):
+    def __init__(self, config, weight_store, device, layers, slots_per_layer: int = 65, prefetch: bool = True,
+                 device_slots: bool = False):
         self.config = config
         self.store = weight_store
         self.device = torch.device(device)
         self.layers = list(layers)
         self.prefetch = prefetch
-        self.gt = GPUTransfer(config, weight_store, self.device, slots_per_layer=slots_per_layer)
+        self.gt = GPUTransfer(config, weight_store, self.device, slots_per_layer=slots_per_layer,
+                              device_slots=device_slots)
         self.cfg = _lib.moe_config(config)
         self.K = config.num_experts_per_tok
         self.ws = torch.zeros(0, dtype=torch.uint8, device=self.device)
@@ -49,6 +51,11 @@ class StreamingDecoder:
         self.min_precision = 0.5
         for layer in self.layers:
             self.gt.bank(layer)
+        # device-managed slot tables: every layer's experts in pinned host memory
+        self.device_slots = device_slots and all(self.gt.device_cache(l) is not None for l in self.layers)
+        if device_slots and not self.device_slots:
+            raise ValueError("device_slots needs every routed expert of the layers in pinned host memory "
+                             "(weight_store.preload_host)")
 
     def _route(self, x, layer, ws, idx, w):
         T = x.shape[0]
@@ -63,6 +70,8 @@ class StreamingDecoder:
 
     def step(self, h: torch.Tensor) -> torch.Tensor:
         """One decode step: h [T, H] bf16 through every layer."""
+        if self.device_slots:
+            return self._step_device(h)
         T = h.shape[0]
         idx = torch.empty(T, self.K, dtype=torch.int64, device=self.device)
         w = torch.empty(T, self.K, dtype=torch.float32, device=self.device)
@@ -96,3 +105,36 @@ class StreamingDecoder:
                 pending_pred = None
             h = x + out
         return h
+
+    def _step_device(self, h: torch.Tensor) -> torch.Tensor:
+        """The decode step with device-managed slot tables: per layer the
+        router, ``dsmoe_slotcache_step`` (slot placement and host->device
+        copies of the missing experts by the SMs) and the expert GEMMs, all
+        enqueued on the current stream; the host reads nothing and waits for
+        nothing. No next-layer prefetch on this path."""
+        T = h.shape[0]
+        idx = torch.empty(T, self.K, dtype=torch.int64, device=self.device)
+        w = torch.empty(T, self.K, dtype=torch.float32, device=self.device)
+        for layer in self.layers:
+            x = h.contiguous()
+            self.ws = self._route(x, layer, self.ws, idx, w)
+            self.gt.device_cache(layer).step(idx)
+            bank = self.gt.bank(layer)
+            out = torch.empty_like(x)
+            lw = _layer_weights(bank, self.store.get_gate_weight(layer), None)
+            check(lib().dsmoe_moe_experts(self.cfg, lw, ptr(x), T, ptr(out), ptr(self.ws), self.ws.numel(),
+                                          stream_handle(self.device)), "dsmoe_moe_experts")
+            h = x + out
+        return h
+
+    def device_counters(self) -> tuple[int, int, int]:
+        """(hits, misses, bytes moved) of the device-managed slot tables (a
+        host read)."""
+        hits = misses = 0
+        for layer in self.layers:
+            a, b = self.gt.device_cache(layer).counters()
+            hits, misses = hits + a, misses + b
+        c = self.config
+        per_expert = 3 * c.hidden_size * c.moe_intermediate_size + \
+            3 * (c.hidden_size // 128) * (c.moe_intermediate_size // 128) * 4
+        return hits, misses, misses * per_expert

@@ -44,6 +44,10 @@ class ExpertCache:
         self.entries.move_to_end(key)
         return entry
 
+    def peek(self, layer: int, expert_idx: int) -> dict | None:
+        """The entry without touching the LRU order or the counters."""
+        return self.entries.get((layer, expert_idx))
+
     def put(self, layer: int, expert_idx: int, expert_dict: dict) -> None:
         need = self.entry_bytes(expert_dict)
         self._evict_until(need)
@@ -164,6 +168,23 @@ class SyntheticWeightStore:
                     entry[p] = {"weight": hw, "weight_scale_inv": hs}
                 self.expert_cache.put(layer, e, entry)
         return total
+
+    def host_expert_pointers(self, layer: int) -> list[int] | None:
+        """Host addresses of every routed expert's six tensors (w_gate,
+        s_gate, w_up, s_up, w_down, s_down) when all of them sit in pinned
+        host memory (after ``preload_host``), else None. The device-side slot
+        cache reads experts from there."""
+        out = []
+        for e in range(self.config.n_routed_experts):
+            ent = self.expert_cache.peek(layer, e)
+            if ent is None:
+                return None
+            for p in PROJS:
+                w, sc = ent[p]["weight"], ent[p]["weight_scale_inv"]
+                if not (w.is_pinned() and sc.is_pinned()):
+                    return None
+                out += [w.data_ptr(), sc.data_ptr()]
+        return out
 
     def device_expert(self, layer: int, e: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
         """Expert ``e`` on the store's device (same bytes as ``get_expert``)."""

@@ -332,6 +332,57 @@ DSMOE_API int dsmoe_expert_ffn_noalloc(const void* x, int32_t tokens, int32_t hi
                                        const void* w_down, const float* s_down, void* out, dsmoe_stream_t stream);
 
 /*
+ * Device-resident expert slot cache for streaming mode (replaces the host side
+ * of GPUTransfer.transfer_experts, inference/gpu_transfer.py:50-89, whose
+ * .tolist() and synchronize() (:60, :79) stop the host once per token and
+ * layer). A layer's routed experts live in pinned host memory; the GPU keeps a
+ * bank of n_slots expert slots (the dsmoe_layer_weights_t layout) and the
+ * group -> slot table the grouped GEMMs read. dsmoe_slotcache_step, called
+ * with the step's routing (the topk_idx of dsmoe_route) before
+ * dsmoe_moe_experts, runs two kernels on `stream`:
+ *   - plan: refresh the recency of the needed experts already in a slot and
+ *     give each missing expert (in id order) the least recently used slot the
+ *     step does not need (empty slots first, ties to the lowest slot, the
+ *     shared expert's slot never), updating slot_of;
+ *   - fill: copy the missing experts' six tensors from host memory (read by
+ *     the SMs over the host link) into their slots.
+ * No host read and no host wait; a step needing more experts than free slots
+ * sets code 4 in *status.
+ * state: dsmoe_slotcache_state_bytes(n_slots) bytes of int32, caller-owned:
+ *   [0] step clock, [1] experts copied by the last step, [2] hits, [3] misses
+ *   (cumulative), then group_in_slot[n_slots] (-1 empty, 0 the shared expert,
+ *   1 + e routed expert e), last_use[n_slots] (-1 empty), and two copy lists
+ *   of n_slots entries. Initialise clock/counters to 0 and group_in_slot /
+ *   last_use to the bank's contents, with slot_of consistent with them.
+ * host_src: device array [n_experts][6] of device-usable addresses of routed
+ *   expert e's w_gate, s_gate, w_up, s_up, w_down, s_down in pinned host
+ *   memory, produced by dsmoe_map_host_pointers from the host addresses.
+ */
+typedef struct {
+  int32_t n_experts;  /* routed experts of the layer (<= 1023) */
+  int32_t n_slots;    /* bank slots, the shared expert's included */
+  int32_t hidden;     /* multiples of 128 */
+  int32_t inter;
+  void* w_gate;       /* bank tensors [n_slots][...], 16-byte aligned */
+  float* s_gate;
+  void* w_up;
+  float* s_up;
+  void* w_down;
+  float* s_down;
+  int32_t* slot_of;   /* [n_experts + 1] group -> slot, -1 absent */
+  int32_t* state;
+  const uint64_t* host_src;
+  int32_t* status;    /* device error word */
+} dsmoe_slotcache_t;
+DSMOE_API size_t dsmoe_slotcache_state_bytes(int32_t n_slots);
+DSMOE_API int dsmoe_slotcache_step(const dsmoe_slotcache_t* cache, const int64_t* topk_idx, int32_t n_pairs,
+                                   dsmoe_stream_t stream);
+/* Host addresses of pinned (page-locked, mapped) host memory -> the addresses
+ * kernels use for it (cudaHostGetDevicePointer); entries must be 16-byte
+ * aligned. Set-up call, host only. */
+DSMOE_API int dsmoe_map_host_pointers(const uint64_t* host_ptrs, int32_t n, uint64_t* dev_ptrs);
+
+/*
  * Next-token sampling, replaces `sample` (inference/engine.py:166-190) and
  * the .item() read of the decode loop (engine.py:116-117, 142-151): the token
  * ids stay on the device.
