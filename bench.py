@@ -281,11 +281,15 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def streaming_measure(local: int, steps: int, warmup: int, prefetch: bool = True) -> dict:
+def streaming_measure(local: int, steps: int, warmup: int, prefetch: bool = True,
+                      modes: tuple[str, ...] = ("device", "host")) -> dict:
     """Config 5: B=1 decode steps through 8 MoE layers (seeds 10..17), all
     routed experts in pinned host memory, a 64-expert GPU slot cache per layer
-    (+ the shared expert), next-layer prefetch on a side stream. Returns the
-    measured figures (device-timed)."""
+    (+ the shared expert). Two ways to run the slot caches, on the same pinned
+    store: "device" (dsmoe_slotcache_step: placement and copies on the GPU, no
+    host read per layer, no prefetch) and "host" (host-side LRU, cudaMemcpyAsync
+    on a side stream, adaptive next-layer prefetch, one routing read-back per
+    layer). Returns the measured figures per mode (device-timed)."""
     from dsmoe import DeepSeekConfig, SyntheticWeightStore
     from dsmoe.streaming import StreamingDecoder
     from dsmoe.synthetic import activations
@@ -312,67 +316,86 @@ def streaming_measure(local: int, steps: int, warmup: int, prefetch: bool = True
     torch.cuda.synchronize()
     link_gbs = 3 * src.nbytes / (c0.elapsed_time(c1) / 1e3) / 1e9
     del src, dst
-    dec = StreamingDecoder(cfg, store, dev, layers, slots_per_layer=65, prefetch=prefetch)
     # a new token every step (N(0,1) hidden state), carried through the 8 layers
     h_host = activations(10, warmup + steps, H).pin_memory()
     out_host = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
-    for i in range(warmup):
-        dec.step(h_host[i:i + 1].to(dev))
-    torch.cuda.synchronize()
-    b0, m0, hit0 = dec.gt.bytes_h2d, dec.gt.slot_misses, dec.gt.slot_hits
-    p0, u0 = dec.predicted, dec.predicted_used
-    sampler = ClockSampler({local})
-    sampler.start()
-    time.sleep(0.3)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_begin = time.time()
-    e0.record()
-    for i in range(steps):
-        hd = h_host[warmup + i: warmup + i + 1].to(dev, non_blocking=True)  # the token in
-        h = dec.step(hd)
-        out_host.copy_(h, non_blocking=True)  # its final hidden state out
-    e1.record()
-    torch.cuda.synchronize()
-    clocks = sampler.stop((t_begin, time.time()))
-    ms = e0.elapsed_time(e1) / steps
-    moved = dec.gt.bytes_h2d - b0
-    misses, hits = dec.gt.slot_misses - m0, dec.gt.slot_hits - hit0
-    achieved = moved / (steps * ms / 1e3) / 1e9
-    out = {"tokens_per_s": 1e3 / ms, "ms_per_step": ms, "steps": steps, "warmup": warmup,
-           "host_link_GB_s": achieved, "pinned_copy_GB_s": link_gbs, "host_link_frac": achieved / link_gbs,
-           "h2d_gb_per_step": moved / steps / 1e9, "slot_hit_rate": hits / max(1, hits + misses),
-           "misses_per_layer_step": misses / (steps * len(layers)),
-           "prefetch_precision": (dec.predicted_used - u0) / max(1, dec.predicted - p0),
-           "prefetched_experts": dec.gt.prefetched, "pinned_host_gb": pinned / 1e9, "host_setup_s": setup_s,
-           "layers": len(layers), "clocks": clocks}
-    del dec, store
+    res = {"pinned_copy_GB_s": link_gbs, "pinned_host_gb": pinned / 1e9, "host_setup_s": setup_s,
+           "layers": len(layers), "steps": steps, "warmup": warmup}
+    for mode in modes:
+        device = mode == "device"
+        dec = StreamingDecoder(cfg, store, dev, layers, slots_per_layer=65, prefetch=prefetch and not device,
+                               device_slots=device)
+
+        def moved_hits_misses():
+            if device:
+                h, m, b = dec.device_counters()
+                return b, h, m
+            return dec.gt.bytes_h2d, dec.gt.slot_hits, dec.gt.slot_misses
+
+        for i in range(warmup):
+            dec.step(h_host[i:i + 1].to(dev))
+        torch.cuda.synchronize()
+        b0, hit0, m0 = moved_hits_misses()
+        p0, u0 = dec.predicted, dec.predicted_used
+        sampler = ClockSampler({local})
+        sampler.start()
+        time.sleep(0.3)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_begin = time.time()
+        e0.record()
+        for i in range(steps):
+            hd = h_host[warmup + i: warmup + i + 1].to(dev, non_blocking=True)  # the token in
+            h = dec.step(hd)
+            out_host.copy_(h, non_blocking=True)  # its final hidden state out
+        e1.record()
+        torch.cuda.synchronize()
+        clocks = sampler.stop((t_begin, time.time()))
+        ms = e0.elapsed_time(e1) / steps
+        b1, hit1, m1 = moved_hits_misses()
+        moved, hits, misses = b1 - b0, hit1 - hit0, m1 - m0
+        achieved = moved / (steps * ms / 1e3) / 1e9
+        res[mode] = {"tokens_per_s": 1e3 / ms, "ms_per_step": ms, "host_link_GB_s": achieved,
+                     "host_link_frac": achieved / link_gbs, "h2d_gb_per_step": moved / steps / 1e9,
+                     "slot_hit_rate": hits / max(1, hits + misses),
+                     "misses_per_layer_step": misses / (steps * len(layers)),
+                     "host_reads_per_layer": 0 if device else 1, "clocks": clocks}
+        if not device:
+            res[mode].update({"prefetch_precision": (dec.predicted_used - u0) / max(1, dec.predicted - p0),
+                              "prefetched_experts": dec.gt.prefetched})
+        del dec
+        torch.cuda.empty_cache()
+    del store
     torch.cuda.empty_cache()
-    return out
+    return res
 
 
 def run_streaming(args, rank, world, local):
-    """Config 5 as its own bench line (``--config 5``)."""
+    """Config 5 as its own bench line (``--config 5``): the device-managed
+    slot caches are the line's value; the host-managed ones are reported
+    beside them."""
     if rank != 0:
         return
     torch.cuda.set_device(local)
     r = streaming_measure(local, args.steps, args.warmup, prefetch=not args.no_prefetch)
+    d = r["device"]
     line = {
-        "metric": METRIC, "value": r["tokens_per_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": d["tokens_per_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": d["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp8-e4m3 (hi/lo activations) x e4m3 weights, fp32 accumulate",
         "data": "synthetic (seeded; per-layer seeds 10..17)",
         "config": {"workload": "B=1 decode through 8 DeepSeek-R1 MoE layers, experts in pinned host memory "
-                               "(config 5), h <- h + moe(h) per layer",
-                   "slots_per_layer": 64, "prefetch": not args.no_prefetch, "pinned_host_gb": r["pinned_host_gb"],
+                               "(config 5), h <- h + moe(h) per layer, device-managed slot caches",
+                   "slots_per_layer": 64, "pinned_host_gb": r["pinned_host_gb"],
                    "host_setup_s": r["host_setup_s"], "baseline_config": 5},
-        "e2e": {"value": r["tokens_per_s"], "unit": UNIT, "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
-        "roofline": {"kernel": "expert H2D copies (host link)", "bound": "host-link", "achieved": r["host_link_GB_s"],
-                     "peak": r["pinned_copy_GB_s"], "unit": "GB/s", "frac": r["host_link_frac"],
-                     "peak_source": "measured pinned->device copy of 1 GiB in this run", "traffic": None},
-        "streaming": {k: r[k] for k in ("h2d_gb_per_step", "slot_hit_rate", "misses_per_layer_step",
-                                        "prefetch_precision", "prefetched_experts")},
-        "gpu_launches": 9 * r["layers"] * args.steps,
-        "clocks": r["clocks"],
+        "e2e": {"value": d["tokens_per_s"], "unit": UNIT, "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
+        "roofline": {"kernel": "expert host->device copies (slot-cache fill kernel)", "bound": "host-link",
+                     "achieved": d["host_link_GB_s"], "peak": r["pinned_copy_GB_s"], "unit": "GB/s",
+                     "frac": d["host_link_frac"], "peak_source": "measured pinned->device copy of 1 GiB in this run",
+                     "traffic": None},
+        "streaming": r,
+        # per layer and step: router 2, slot plan + fill 2, count/plan/scatter 3, GEMMs 2, swiglu 1, combine 1
+        "gpu_launches": 11 * r["layers"] * args.steps,
+        "clocks": d["clocks"],
         "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)

@@ -25,17 +25,17 @@
 // row is [g | u] (2F wide); swiglu_quant.cu forms h = silu(g) * u.
 //
 // Warp roles (one CTA per SM, persistent over work units):
-//   warp 0      TMA producer (one thread); also prefetches the weight tiles
-//               PF_DIST K steps ahead into L2, across unit boundaries
+//   warp 0      TMA producer (one thread)
 //   warp 1      TMEM allocator + MMA issuer for even K steps (one thread)
 //   warp 2      MMA issuer for odd K steps (one thread)
 //   warp 3      unit planner: decodes the CTA's work units ahead of time into
 //               a shared-memory ring (rows, weight row, MMA width and the
 //               unit's first 32 weight scales), so that no other role waits on
 //               a chain of dependent global loads at a unit boundary
-//   warps 4..   epilogue, EPI_WARPS of them: warp w reads TMEM lane quadrant
-//               (w % 4) and one column group of BN / (EPI_WARPS / 4) (<= 32)
-//               columns, in TMEM loads of up to 16 columns per term.
+//   warps 4..   epilogue, 16 warps: warp w reads TMEM lane quadrant (w % 4)
+//               and one column group of BN / 4 columns; a K step's partial
+//               (40 columns at BN 160) is read with all its TMEM loads in
+//               flight together and one wait.
 // Two issuers: a thread that waits on an mbarrier between its MMA batches
 // leaves the tensor pipe idle for a few hundred cycles each time; with the
 // K steps split by parity one issuer's MMAs run while the other waits. Every
@@ -61,7 +61,6 @@ constexpr int SUB = 32;   // token rows per small activation TMA box
 constexpr int MAX_GROUPS = 264;
 constexpr int RING = 4;       // unit-plan entries in flight
 constexpr int SW_WIN = 32;    // weight scales per window (one per lane)
-constexpr int PF_DIST = 8;    // K steps of L2 prefetch ahead of the TMA loads
 constexpr int PLAN_WARP = 3;
 constexpr int EPI_WARP0 = 4;
 
@@ -93,9 +92,9 @@ struct Cfg {
   static constexpr int NUM_THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
   static constexpr int TCOLS = NCAT ? 2 * BN : BN;  // TMEM columns per buffer
   static constexpr int EPI_COLS = BN / NUM_CG;    // accumulator columns per epilogue warp
-  // columns per TMEM load (16 keeps the 768-thread kernel within its 80
-  // registers per thread without spills)
-  static constexpr int CHUNK = EPI_COLS < 16 ? EPI_COLS : 16;
+  // columns per TMEM load: the warp's whole slice where the partial is one
+  // term, 16-column pieces of hi and lo where it is two
+  static constexpr int CHUNK = NCAT ? (EPI_COLS < 16 ? EPI_COLS : 16) : EPI_COLS;
   static constexpr int XH_OFF = BM * BK;
   static constexpr int XL_OFF = XH_OFF + BN * BK;
   static constexpr int STAGE_BYTES = XL_OFF + BN * BK;  // multiple of 1024 for BN % 8 == 0
@@ -108,7 +107,8 @@ struct Cfg {
   static constexpr int PLAN_OFF = ((MISC_OFF + 16 + 15) / 16) * 16;
   static constexpr int SMEM_BYTES = PLAN_OFF + RING * static_cast<int>(sizeof(UnitPlan)) + 1024;  // + alignment slack
   static_assert(EPI_WARPS % 4 == 0 && BN % NUM_CG == 0, "epilogue split");
-  static_assert(EPI_COLS <= 32 && (CHUNK == 8 || CHUNK == 16) && EPI_COLS % CHUNK == 0, "epilogue columns");
+  static_assert(EPI_COLS <= 40 && (CHUNK == 8 || CHUNK == 16 || CHUNK == 32 || CHUNK == 40) &&
+                    EPI_COLS % CHUNK == 0, "epilogue columns");
   static_assert(BN % 32 == 0 && BN <= 256 && NBUF * TCOLS <= 512 && (!NCAT || 2 * BN <= 256), "tile shape");
   static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
@@ -132,15 +132,12 @@ __device__ __forceinline__ void decode_unit(int u, int n_groups, const int* __re
 
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v) {
-  if constexpr (N == 16) tmem_ld16(taddr, v);
+  if constexpr (N == 40) {
+    tmem_ld32(taddr, v);
+    tmem_ld8(taddr + 32, v + 32);
+  } else if constexpr (N == 32) tmem_ld32(taddr, v);
+  else if constexpr (N == 16) tmem_ld16(taddr, v);
   else tmem_ld8(taddr, v);
-}
-
-// Bring one weight tile (128 rows x 128 bytes) into L2 ahead of its TMA load.
-__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
-               : "memory");
 }
 
 template <int BN_, int STAGES_, int NBUF_, bool NCAT_, int EPI_WARPS_>
@@ -248,7 +245,6 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      int pf_done = 0;  // K steps of the current unit already prefetched into L2
       bool ok = true;
       int i = 0;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++i) {
@@ -256,22 +252,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         if (!mbar_wait(&ufull[ri], (i / RING) & 1, p.status, kDevTimeoutProducer, s_abort)) break;
         const UnitPlan* e = plan + ri;
         const int ncols = e->ncols, row0 = e->row0, wrow = e->wrow, mat = e->mat;
-        // The next unit's weight rows, when its plan is already there (no
-        // wait), for the L2 prefetch that runs past the end of this unit. Its
-        // entry cannot be reused before this thread releases it.
-        int nwrow = -1, nmat = 0;
-        if (u + static_cast<int>(gridDim.x) < total_units) {
-          const int rn = (i + 1) % RING;
-          if (mbar_try_wait(&ufull[rn], ((i + 1) / RING) & 1)) {
-            nwrow = plan[rn].wrow;
-            nmat = plan[rn].mat;
-          }
-        }
         mbar_arrive(&uempty[ri]);
         const CUtensorMap* tw = mat ? &tm_w1 : &tm_w0;
-        const CUtensorMap* twn = nmat ? &tm_w1 : &tm_w0;
-        for (int kb = pf_done; kb < PF_DIST && kb < n_kb; ++kb) tma_prefetch_l2(tw, kb * BK, wrow);
-        int next_pf = 0;
         const int nsub = (ncols + SUB - 1) / SUB;
         // A few 32-row boxes beat one big box; four or more cost more than the
         // rows they save (a 128-token tile as 4 boxes: +8% kernel time).
@@ -292,17 +274,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
             tma_load_2d(st + C::XH_OFF, &tm_x, &full[stage], kb * BK, row0, pol_x);
             tma_load_2d(st + C::XL_OFF, &tm_x, &full[stage], kb * BK, p.P + row0, pol_x);
           }
-          const int pk = kb + PF_DIST;
-          if (pk < n_kb) {
-            tma_prefetch_l2(tw, pk * BK, wrow);
-          } else if (nwrow >= 0 && pk - n_kb < n_kb) {
-            tma_prefetch_l2(twn, (pk - n_kb) * BK, nwrow);
-            next_pf = pk - n_kb + 1;
-          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        pf_done = next_pf;
       }
       // Drain: the copies of the last issued stages must have landed before
       // the CTA may exit (normally they were consumed already).
@@ -392,10 +366,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       const float* wsc = (mat ? p.wscale1 : p.wscale0) + wsc_off;
       float swr1 = 32 + lane < n_kb ? __ldg(wsc + 32 + lane) : 0.f;
       const int nvalid = max(0, min(EPI_COLS, ncols - c0));  // valid columns of this warp
-      // Per-row activation scale of this warp's column `lane`, loaded now so
-      // that the latency hides behind the K loop.
+      // Per-row activation scales of this warp's columns `lane` and
+      // `32 + lane`, loaded now so that the latency hides behind the K loop.
       const int row_base = row0 + c0;
       const float sxv = lane < nvalid ? __ldg(p.sx + row_base + lane) : 0.f;
+      const float sxw = 32 + lane < nvalid ? __ldg(p.sx + row_base + 32 + lane) : 0.f;
       float acc[EPI_COLS];
 #pragma unroll
       for (int c = 0; c < EPI_COLS; ++c) acc[c] = 0.f;
@@ -446,8 +421,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
       __nv_bfloat16* ybase = p.y + mat * p.M + row_in_mat;
 #pragma unroll
       for (int c = 0; c < EPI_COLS; c += 2) {
-        const float s0 = __shfl_sync(0xffffffffu, sxv, c);
-        const float s1 = __shfl_sync(0xffffffffu, sxv, c + 1);
+        const float s0 = __shfl_sync(0xffffffffu, c < 32 ? sxv : sxw, c & 31);
+        const float s1 = __shfl_sync(0xffffffffu, c + 1 < 32 ? sxv : sxw, (c + 1) & 31);
         const __nv_bfloat16 v0 = __float2bfloat16_rn(acc[c] * s0);
         const __nv_bfloat16 v1 = __float2bfloat16_rn(acc[c + 1] * s1);
         const unsigned short mine = __bfloat16_as_ushort(odd ? v1 : v0);
@@ -507,7 +482,7 @@ cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, co
     case 32: return gg::launch_cfg<32, 8, 8, true, 16>(w0, w1, x, x32, p, grid, stream);
     case 64: return gg::launch_cfg<64, 6, 4, true, 16>(w0, w1, x, x32, p, grid, stream);
     case 128: return gg::launch_cfg<128, 4, 2, true, 16>(w0, w1, x, x32, p, grid, stream);
-    case 160: return gg::launch_cfg<160, 4, 3, false, 20>(w0, w1, x, x32, p, grid, stream);
+    case 160: return gg::launch_cfg<160, 4, 3, false, 16>(w0, w1, x, x32, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
