@@ -60,9 +60,13 @@ def _rank_main(rank, world, port, q):
             ref.append((x, layer.forward(x)))
         layer.use_peer_memory(cap=256)
         try:
-            for x, want in ref:
-                got = layer.forward(x)
-                results.append(0.0 if torch.equal(got, want) else 1.0)
+            for overlap in (False, True):  # pushes in order, then on a side stream beside the shared expert
+                layer.overlap = overlap
+                for x, want in ref:
+                    got = layer.forward(x)
+                    results.append(0.0 if torch.equal(got, want) else 1.0)
+            torch.cuda.synchronize()
+            results.append(float(layer.push_status()))  # 0: every pushed row fit the receive buffers
         finally:
             layer.close()
         dist.barrier()
