@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(const int64_t* __res
       }
     }
     __syncthreads();
-    if (tid == 0) s_nmiss = placed;  // placed so far (broadcast for the next round)
+    if (tid == 0) s_nmiss = placed;  // placed so far (broadcast for the next miss)
     __syncthreads();
     placed = s_nmiss;
   }
