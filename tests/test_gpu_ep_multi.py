@@ -52,19 +52,29 @@ def _rank_main(rank, world, port, q):
             out = layer.forward(x, chunks=chunks)
             single = moe_block(x, 3, store, gt, cfg)
             results.append(rel_rms(out.float().cpu(), single.float().cpu()))
-        # the same steps through the peer-memory exchange: bit-identical outputs
+        # The same steps through the peer-memory exchange. Its expert GEMMs
+        # choose their token tile from the capacity bound (2 ranks x cap = 512
+        # rows -> the 160-token tile, which sums the hi and lo activation
+        # terms in one accumulator), the all-to-all step's from the rows it
+        # received (the 32- to 128-token tiles keep the two terms in separate
+        # accumulator columns). At T=200 a rank receives ~390 rows, the same
+        # tile, so the outputs must be bit-identical; at T=64 and T=1 they may
+        # round differently and are held to the single-GPU block's tolerance.
         ref = []
         for step, T in enumerate((64, 200, 1)):
             x = activations(500 + step + 10 * rank, T, 512).to(dev)
             layer.overlap, layer.sm_reserve = False, 0
-            ref.append((x, layer.forward(x)))
+            ref.append((x, layer.forward(x), moe_block(x, 3, store, gt, cfg)))
         layer.use_peer_memory(cap=256)
         try:
             for overlap in (False, True):  # pushes in order, then on a side stream beside the shared expert
                 layer.overlap = overlap
-                for x, want in ref:
+                for x, want, single in ref:
                     got = layer.forward(x)
-                    results.append(0.0 if torch.equal(got, want) else 1.0)
+                    if x.shape[0] == 200:
+                        results.append(0.0 if torch.equal(got, want) else 1.0)
+                    else:
+                        results.append(rel_rms(got.float().cpu(), single.float().cpu()))
             torch.cuda.synchronize()
             results.append(float(layer.push_status()))  # 0: every pushed row fit the receive buffers
         finally:
