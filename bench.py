@@ -469,7 +469,7 @@ def main():
     from datetime import timedelta
 
     from dsmoe import DeepSeekConfig, GPUTransfer, SyntheticWeightStore, moe_block
-    from dsmoe._lib import Workspace, set_profile_events
+    from dsmoe._lib import ClockProbe, Workspace, set_profile_events
     from dsmoe.ep import PEER_PHASES
     from dsmoe.synthetic import activations
 
@@ -538,7 +538,9 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    probe = ClockProbe(dev)  # the SMs' own cycle counters across the timed region
     t_begin = time.time()
+    probe.start()
     e0.record()
     for i in range(args.steps):
         if ep:  # the library's events around the rank's expert GEMMs only
@@ -548,6 +550,7 @@ def main():
             set_profile_events(evsets[i])
         step(x)
     e1.record()
+    probe.stop()
     torch.cuda.synchronize()
     t_end = time.time()
     if ep:
@@ -557,6 +560,10 @@ def main():
     if world > 1:
         dist.barrier()
     clocks = sampler.stop((t_begin, t_end)) if rank == 0 else None
+    if rank == 0:
+        clocks = clocks or {}
+        # mean SM clock over the timed steps from the SMs' cycle counters (median over SMs)
+        clocks["sm_mhz_device"] = probe.mhz()
     ms = e0.elapsed_time(e1) / args.steps
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -591,6 +598,14 @@ def main():
             pbm = ep_layer.peer.views["meta"].view(torch.int32)
             lidx = pbm[: world * ep_layer.peer.cap * TOPK].view(-1, TOPK)[:rows_recv].reshape(-1)
             ep_phases["rows_per_rank_received"] = rows_recv
+            # load balance across ranks (skewed routing concentrates rows on the
+            # ranks owning the hot experts)
+            rr = torch.tensor([rows_recv], dtype=torch.int64, device=dev)
+            rr_all = [torch.zeros_like(rr) for _ in range(world)]
+            dist.all_gather(rr_all, rr)
+            rows_all = [int(t.item()) for t in rr_all]
+            ep_phases["rows_received_by_rank"] = rows_all
+            ep_phases["rows_received_max_over_mean"] = max(rows_all) / (sum(rows_all) / world)
         lidx = lidx[lidx >= 0].long()
     config3 = None
     if args.extra_config3:

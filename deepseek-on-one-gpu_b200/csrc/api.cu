@@ -379,6 +379,13 @@ int dsmoe_set_profile_events(void* const* events, int32_t n) {
   return DSMOE_OK;
 }
 
+int dsmoe_clock_probe(uint64_t* out, int32_t n_slots, dsmoe_stream_t stream) {
+  if (!out || n_slots < num_sms()) return fail(DSMOE_ERR_INVALID, "clock probe: %d slots for %d SMs", n_slots, num_sms());
+  DSMOE_CUDA(launch_clock_probe(reinterpret_cast<unsigned long long*>(out), n_slots, num_sms(),
+                                reinterpret_cast<cudaStream_t>(stream)));
+  return DSMOE_OK;
+}
+
 int dsmoe_set_gemm_sm_limit(int32_t max_ctas) {
   if (max_ctas < 0) return fail(DSMOE_ERR_INVALID, "max_ctas < 0");
   g_gemm_ctas = max_ctas;

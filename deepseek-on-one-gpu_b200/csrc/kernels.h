@@ -41,6 +41,10 @@ int gemm_tile_tokens(int tokens);
 cudaError_t launch_grouped_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& x,
                                 const CUtensorMap& x32, const GemmParams& p, int tile, int grid, cudaStream_t stream);
 
+// Clock probe (clockprobe.cu): out[2*smid] = SM cycle counter, out[2*smid+1] =
+// global ns timer, for every SM a block lands on (smid < n_slots).
+cudaError_t launch_clock_probe(unsigned long long* out, int n_slots, int n_sm, cudaStream_t stream);
+
 // SwiGLU + hi/lo split (swiglu_quant.cu)
 // rows of real (token, group) pairs only: row_start[n_groups + 1], counts[n_groups]
 cudaError_t launch_swiglu_quant(const __nv_bfloat16* gu, int F, const int32_t* row_start, const int32_t* counts,

@@ -27,6 +27,7 @@ EXPORTED = (
     "dsmoe_moe_layer_ffn", "dsmoe_read_ranges", "dsmoe_ep_plan", "dsmoe_ep_push", "dsmoe_moe_local_peer",
     "dsmoe_ep_meta_bytes", "dsmoe_ipc_alloc", "dsmoe_ipc_open", "dsmoe_ipc_close", "dsmoe_ipc_free",
     "dsmoe_sample_top_p", "dsmoe_slotcache_state_bytes", "dsmoe_slotcache_step", "dsmoe_map_host_pointers",
+    "dsmoe_clock_probe",
 )
 
 
@@ -91,6 +92,7 @@ def lib() -> ctypes.CDLL:
                 L.dsmoe_fp8_linear.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, sz, vp]
                 L.dsmoe_read_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int32), vp]
                 L.dsmoe_set_profile_events.argtypes = [ctypes.POINTER(vp), i32]
+                L.dsmoe_clock_probe.argtypes = [vp, i32, vp]
                 L.dsmoe_expert_ffn_noalloc.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]
                 L.dsmoe_ep_dispatch.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]
                 L.dsmoe_moe_local_workspace_size.argtypes = [cfgp, i32]
@@ -195,6 +197,40 @@ def set_gemm_sm_limit(max_ctas: int) -> None:
     per SM; 0 = all SMs) so that a collective on another stream finds free
     SMs."""
     check(lib().dsmoe_set_gemm_sm_limit(int(max_ctas)), "dsmoe_set_gemm_sm_limit")
+
+
+class ClockProbe:
+    """Mean SM clock over a region of a stream: ``start()`` and ``stop()``
+    enqueue a probe in which every SM records its cycle counter and the
+    global ns timer; ``mhz()`` (after the stream is synchronised) is the
+    median over SMs of cycles / ns between the two."""
+
+    def __init__(self, device):
+        import torch
+
+        self.n = torch.cuda.get_device_properties(device).multi_processor_count
+        self.a = torch.zeros(2 * self.n, dtype=torch.int64, device=device)
+        self.b = torch.zeros_like(self.a)
+
+    def _probe(self, buf):
+        import torch
+
+        check(lib().dsmoe_clock_probe(buf.data_ptr(), self.n, torch.cuda.current_stream(buf.device).cuda_stream),
+              "dsmoe_clock_probe")
+
+    def start(self):
+        self._probe(self.a)
+
+    def stop(self):
+        self._probe(self.b)
+
+    def mhz(self) -> float | None:
+        a, b = self.a.view(-1, 2).cpu().double(), self.b.view(-1, 2).cpu().double()
+        dt = b[:, 1] - a[:, 1]
+        ok = (a[:, 1] > 0) & (b[:, 1] > 0) & (dt > 0)
+        if not bool(ok.any()):
+            return None
+        return float(((b[:, 0] - a[:, 0])[ok] / dt[ok]).median() * 1e3)
 
 
 def set_profile_events(events: list | None) -> None:

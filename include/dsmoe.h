@@ -153,6 +153,15 @@ DSMOE_API int dsmoe_fp8_linear(const void* x, int32_t tokens, int32_t in_feature
 DSMOE_API int dsmoe_set_profile_events(void* const* events, int32_t n);
 
 /*
+ * Measurement hook (no reference counterpart): enqueues on `stream` a probe in
+ * which every SM writes its cycle counter and the global nanosecond timer to
+ * out[2*smid] and out[2*smid+1] (device memory, n_slots pairs, n_slots >= the
+ * SM count). Two probes around a timed region give each SM's mean clock over
+ * it: (cycles after - before) / (ns after - before).
+ */
+DSMOE_API int dsmoe_clock_probe(uint64_t* out, int32_t n_slots, dsmoe_stream_t stream);
+
+/*
  * RMSNorm, replaces `rms_norm` (inference/ops.py:10-13):
  *   out = bf16( bf16(x * 1/sqrt(mean(x^2) + eps)) * weight )
  * x, out [tokens][hidden] bf16, weight [hidden] bf16, hidden % 8 == 0, all
