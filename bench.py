@@ -640,6 +640,21 @@ def main():
         counts = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).cpu()
         touched = int((counts > 0).sum()) + 1  # + shared expert
         rows = T * TOPK + T
+    gu_ms, dn_ms = stage_ms[2], stage_ms[4]
+    crit_rank, gemm_ms_by_rank = 0, None
+    if ep:
+        # The roofline is the critical rank's: under skewed routing some ranks
+        # get few rows (or none: at 8 ranks a rank owns exactly one expert
+        # group, which group-limited routing can skip entirely).
+        mine = torch.tensor([float(rows), float(touched)] + list(stage_ms), dtype=torch.float64, device=dev)
+        allv = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allv, mine)
+        allv = [v.tolist() for v in allv]
+        gemm_ms_by_rank = [round(v[2 + 2] + v[2 + 4], 4) for v in allv]
+        crit_rank = max(range(world), key=lambda r: gemm_ms_by_rank[r])
+        rows, touched = int(allv[crit_rank][0]), int(allv[crit_rank][1])
+        stage_ms = allv[crit_rank][2:]
+        gu_ms, dn_ms = stage_ms[2], stage_ms[4]
     w13 = 2 * F * H + 2 * (F // 128) * (H // 128) * 4
     w2 = F * H + (F // 128) * (H // 128) * 4
     # algorithmic bytes per launch: weights of every expert used, activations
@@ -649,7 +664,6 @@ def main():
     down_bytes = touched * w2 + rows * (F * 2 + (F // 128) * 4) + rows * H * 2
     algo_flops = 2.0 * rows * 3 * F * H  # useful FP8-GEMM work (hi/lo doubles what the tensor pipe executes)
     hbm_peak, bf16_peak, bf16_sustained, peak_src = peaks()
-    gu_ms, dn_ms = stage_ms[2], stage_ms[4]
     dominant = "gate_up" if gu_ms >= dn_ms else "down"
     dom_bytes, dom_ms = (gateup_bytes, gu_ms) if dominant == "gate_up" else (down_bytes, dn_ms)
     dom_flops = 2.0 * rows * (2 * F if dominant == "gate_up" else F) * H  # algorithmic (one pass over x)
@@ -660,8 +674,9 @@ def main():
     # the FP8 rate / 2 = the measured bf16 GEMM rate; sustained, because the
     # kernel is timed inside a long step under the 1000 W cap.
     tensor_roof = bf16_sustained
+    dom_ms = max(dom_ms, 1e-6)
     hbm_frac = dom_bytes / (dom_ms / 1000.0) / 1e9 / hbm_peak
-    if dom_flops / dom_bytes > tensor_roof * 1e12 / (hbm_peak * 1e9):
+    if dom_bytes > 0 and dom_flops / dom_bytes > tensor_roof * 1e12 / (hbm_peak * 1e9):
         achieved = dom_flops / (dom_ms / 1000.0) / 1e12
         roofline = {"kernel": f"grouped_gemm_kernel ({dominant})", "bound": "tensor", "achieved": achieved,
                     "peak": tensor_roof, "unit": "TFLOP/s", "frac": achieved / tensor_roof,
@@ -676,6 +691,9 @@ def main():
                     "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
                     "algorithmic_flops_per_launch": dom_flops,
                     "tensor_frac": dom_flops / (dom_ms / 1000.0) / 1e12 / tensor_roof}
+    if ep:
+        roofline["rank"] = crit_rank  # the rank whose expert GEMMs took longest
+        roofline["gemm_ms_by_rank"] = gemm_ms_by_rank
     roofline["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch on this "
                                   "workload (profiles/)" if traffic else None)
     roofline["timing"] = ("mean of the launch's CUDA-event duration over the timed steps (events recorded by the "
@@ -855,6 +873,7 @@ def main():
                               "overlapping the neighbouring steps' compute"},
             "roofline": roofline,
             "stages_ms": {nm: v for nm, v in zip(names, stage_ms) if nm},
+            "stages_rank": crit_rank if ep else None,
             "stages_sum_over_step": None if ep else sum(stage_ms) / ms_max,
             **({"config3_t8192": config3} if config3 else {}),
             **({"ep_phases_ms": ep_phases} if ep_phases else {}),

@@ -228,7 +228,13 @@ class EPLayer:
         self._flag = None
         self.overlap = True  # CUDA tensors: exchange on a side stream, shared expert while rows travel
         self.sm_reserve = 0  # SMs left to the collectives while GEMMs and all-to-alls overlap
-        self.push_sms = 16  # peer-memory step: SMs the shared expert leaves to the row pushes (0 = no overlap)
+        # peer-memory step: SMs the shared expert leaves to the row pushes (0 =
+        # no overlap). The rows a rank sends to other GPUs grow with the world
+        # size (at T tokens: ~T rows at 2 ranks, ~2.2 T at 4, ~3.5 T at 8) and
+        # SM-issued stores to a peer reach ~9 GB/s per CTA up to ~690 GB/s, so
+        # the share grows with it until pushes and shared expert take about
+        # equally long.
+        self.push_sms = {1: 16, 2: 8, 4: 14}.get(world, min(32, 2 + 5 * world // 2))
         self._push_status = None
         # Optional timing of the peer-memory step (CUDA events recorded on the
         # compute stream): phase_events[0..6] at the PEER_PHASES boundaries,
