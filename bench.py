@@ -433,6 +433,8 @@ def main():
     ap.add_argument("--no-overlap", action="store_true",
                     help="expert-parallel step: exchange and GEMMs in one stream, one after the other")
     ap.add_argument("--ref-tokens-per-step", type=int, default=8)
+    ap.add_argument("--ep-placement", default="auto", choices=["auto", "contiguous", "balanced"],
+                    help="expert placement over ranks at N>1 (auto: balanced when routing is skewed)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--experts", type=int, default=E, help="routed experts (32 per group); smaller = profiling case")
     ap.add_argument("--skip-e2e", action="store_true")
@@ -500,6 +502,28 @@ def main():
             ep_layer.use_peer_memory(cap=max(T, 8192 if args.extra_config3 else 0))
         bank = None
         x = activations(1000 * seed + rank, T, H, device=dev)
+        # Expert placement: contiguous ranges unless the routing of this
+        # step's tokens (counted over all ranks) would load the busiest rank
+        # more than 1.25x the mean, as skewed routing does; then experts are
+        # spread by load (dsmoe.ep.balanced_placement), every rank alike.
+        from dsmoe.ep import balanced_placement
+        cal_idx, _ = ep_layer.route(x)
+        loads = torch.bincount(cal_idx.reshape(-1), minlength=cfg.n_routed_experts).double()
+        dist.all_reduce(loads)
+        loads = loads.cpu()
+        El = cfg.n_routed_experts // world
+        rank_loads = loads.view(world, El).sum(1)
+        contiguous_imbalance = float(rank_loads.max() / rank_loads.mean())
+        placement_info = {"placement": "contiguous", "expected_rank_load_max_over_mean": contiguous_imbalance}
+        if args.ep_placement == "balanced" or (args.ep_placement == "auto" and contiguous_imbalance > 1.25):
+            placement = balanced_placement(loads.tolist(), world)
+            ep_layer.set_placement(placement)
+            bal = torch.zeros(world, dtype=torch.float64)
+            for e, pos in enumerate(placement):
+                bal[pos // El] += loads[e]
+            placement_info = {"placement": "balanced by expert load (longest-processing-time rule)",
+                              "expected_rank_load_max_over_mean": float(bal.max() / bal.mean()),
+                              "contiguous_expected_rank_load_max_over_mean": contiguous_imbalance}
 
         def step(inp):
             return ep_layer.forward(inp, chunks=args.chunks)
@@ -877,6 +901,7 @@ def main():
             "stages_sum_over_step": None if ep else sum(stage_ms) / ms_max,
             **({"config3_t8192": config3} if config3 else {}),
             **({"ep_phases_ms": ep_phases} if ep_phases else {}),
+            **({"ep_placement": placement_info} if ep else {}),
             "layer": {"algorithmic_bytes": layer_bytes, "GB_s": layer_bytes / (layer_ms / 1e3) / 1e9,
                       "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / hbm_peak,
                       "fp8_tflops_algorithmic": algo_flops / (ms_max / 1e3) / 1e12,

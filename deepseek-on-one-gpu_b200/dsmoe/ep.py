@@ -196,6 +196,29 @@ def local_config(config, world: int):
     return config.with_(n_routed_experts=El, n_group=ng, topk_group=ng)
 
 
+def balanced_placement(loads, world: int) -> list[int]:
+    """Expert placement for skewed routing: ``loads[e]`` is expert e's expected
+    number of (token, expert) pairs (e.g. counted over a calibration batch).
+    Experts are taken in decreasing load and each goes to the rank with the
+    smallest load so far among ranks with a free slot (E / world slots each):
+    the longest-processing-time rule. Returns ``placement`` with
+    ``placement[e] = rank * (E / world) + slot``, a permutation of range(E)."""
+    loads = [float(v) for v in loads]
+    E = len(loads)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    El = E // world
+    rank_load = [0.0] * world
+    used = [0] * world
+    placement = [0] * E
+    for e in sorted(range(E), key=lambda i: (-loads[i], i)):
+        r = min((q for q in range(world) if used[q] < El), key=lambda q: (rank_load[q], q))
+        placement[e] = r * El + used[r]
+        used[r] += 1
+        rank_load[r] += loads[e]
+    return placement
+
+
 PEER_PHASES = ("route_plan_count_gather", "push_beside_shared_expert", "barrier_rows_landed",
                "expert_gemms_partials_return", "barrier_partials_back", "combine")
 
@@ -203,10 +226,14 @@ PEER_PHASES = ("route_plan_count_gather", "push_beside_shared_expert", "barrier_
 class EPLayer:
     """One MoE layer, expert-parallel. ``expert_source(layer, e)`` returns expert
     ``e``'s ``{proj: (weight, scale)}`` (any device); by default the weight
-    store's ``get_expert``."""
+    store's ``get_expert``. ``placement`` (optional, every rank the same):
+    expert e lives on rank ``placement[e] // El`` in its slot
+    ``placement[e] % El``; by default rank r owns experts ``[r*El, (r+1)*El)``.
+    The router's expert ids are relabelled through it on the device, so the
+    exchange kernels see contiguous ranges either way."""
 
     def __init__(self, config, weight_store, device, layer: int, world: int, rank: int, exchange=None,
-                 expert_source=None):
+                 expert_source=None, placement=None):
         self.config = config
         self.store = weight_store
         self.device = torch.device(device)
@@ -215,12 +242,11 @@ class EPLayer:
         self.exchange = exchange
         self.lcfg = local_config(config, world)
         self.El = self.lcfg.n_routed_experts
-        src = expert_source or weight_store.get_expert
+        self._src = expert_source or weight_store.get_expert
         self.bank = LayerBank(self.lcfg, self.El + 1, self.device)
         self.bank.write_slot(self.bank.assign(0), weight_store.get_shared_expert_weights(layer))
-        for el in range(self.El):
-            self.bank.write_slot(self.bank.assign(el + 1), src(layer, rank * self.El + el))
-        self.bank.sync_table(non_blocking=False)
+        self.relabel = None  # device int64 [E]: router expert id -> rank * El + slot
+        self.set_placement(placement)
         self.shared = {p: (self.bank.w[p][0], self.bank.s[p][0]) for p in PROJS}
         self._ws = torch.zeros(0, dtype=torch.uint8, device=self.device)
         self._comm = None  # side stream of the overlapped step
@@ -243,11 +269,36 @@ class EPLayer:
         self.lib_events = None
         self.last_counts_all = None
 
+    def set_placement(self, placement=None) -> None:
+        """(Re)load this rank's experts for ``placement`` (see the class
+        docstring; None = contiguous ranges). Every rank must use the same."""
+        E, El = self.config.n_routed_experts, self.El
+        if placement is None:
+            owned = [self.rank * El + el for el in range(El)]
+            self.relabel = None
+        else:
+            placement = [int(v) for v in placement]
+            if sorted(placement) != list(range(E)):
+                raise ValueError("placement must be a permutation of the expert ids")
+            inv = [0] * E
+            for e, pos in enumerate(placement):
+                inv[pos] = e
+            owned = [inv[self.rank * El + el] for el in range(El)]
+            self.relabel = torch.tensor(placement, dtype=torch.int64, device=self.device)
+        for el, e in enumerate(owned):
+            # local expert el is group el + 1 of the rank's bank (group 0: shared)
+            self.bank.write_slot(self.bank.assign(el + 1), self._src(self.layer, e))
+        self.bank.sync_table(non_blocking=False)
+        self.owned = owned
+
     # -------------------------------------------------------------- phases
     def route(self, x: torch.Tensor):
         cfg = self.config
         bias = self.store.get_gate_bias(self.layer) if getattr(cfg, "router_mode", "ref") == "v3" else None
-        return route(x, self.store.get_gate_weight(self.layer), cfg, score_bias=bias)
+        idx, w = route(x, self.store.get_gate_weight(self.layer), cfg, score_bias=bias)
+        if self.relabel is not None:
+            idx = self.relabel[idx]  # rank * El + slot: contiguous ranges for the exchange kernels
+        return idx, w
 
     def dispatch(self, x: torch.Tensor):
         """Route and pack. Returns (counts[W] int32 device, tok_rows, send_x, send_meta)."""

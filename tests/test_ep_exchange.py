@@ -69,3 +69,35 @@ def test_dist_exchange_gloo_ranks(world):
     for p in procs:
         p.join(timeout=60)
     assert results == {r: "ok" for r in range(world)}
+
+
+def test_balanced_placement_is_a_permutation_with_equal_slots_and_spreads_load():
+    """balanced_placement (longest-processing-time rule): a permutation of the
+    expert ids, E / W experts per rank, and under Zipf-skewed loads the busiest
+    rank within the rule's bound (mean + the largest single load)."""
+    import random
+
+    from dsmoe.ep import balanced_placement
+
+    E = 256
+    for W in (2, 4, 8):
+        rng = random.Random(W)
+        loads = [1.0 / (i + 1) ** 1.1 for i in range(E)]
+        rng.shuffle(loads)
+        p = balanced_placement(loads, W)
+        assert sorted(p) == list(range(E))
+        El = E // W
+        per_rank = [0] * W
+        load = [0.0] * W
+        for e, pos in enumerate(p):
+            per_rank[pos // El] += 1
+            load[pos // El] += loads[e]
+        assert per_rank == [El] * W
+        mean = sum(loads) / W
+        assert max(load) <= mean + max(loads) + 1e-12
+        # contiguous ranges over the same (shuffled) loads are worse or equal
+        contiguous = [sum(loads[r * El:(r + 1) * El]) for r in range(W)]
+        assert max(load) <= max(contiguous) + 1e-12
+    # uniform loads keep every rank equal
+    p = balanced_placement([1.0] * E, 8)
+    assert sorted(p) == list(range(E))

@@ -38,6 +38,44 @@ def test_ep_emulated_matches_single_gpu(W, T, mode):
         assert O.rel_rms(outs[r].float().cpu(), ref.float()) < REL_RMS_TOL
 
 
+def test_ep_emulated_balanced_placement_matches_single_gpu():
+    """Skewed routing (bias-corrected router, Zipf expert bias) with the experts
+    placed by load (dsmoe.ep.balanced_placement): each rank holds the experts
+    the placement gives it, the router's ids are relabelled on the device, and
+    every rank's output matches the single-GPU block."""
+    from dsmoe.ep import balanced_placement
+
+    H, F = 512, 256
+    cfg = DeepSeekConfig(hidden_size=H, moe_intermediate_size=F, router_mode="v3")
+    store = SyntheticWeightStore(cfg, seed=31, device=DEV, pin_memory=False, gen_device="cpu", bias_zipf=1.1)
+    W, T = 8, 300
+    xs = [activations(40 + r, T, H).to(DEV) for r in range(W)]
+    probe = EPLayer(cfg, store, DEV, 3, W, 0, expert_source=store.device_expert)
+    loads = sum(torch.bincount(probe.route(x)[0].reshape(-1), minlength=256) for x in xs).double().cpu()
+    placement = balanced_placement(loads.tolist(), W)
+    El = 256 // W
+    contiguous = loads.view(W, El).sum(1)
+    spread = torch.zeros(W, dtype=torch.float64)
+    for e, pos in enumerate(placement):
+        spread[pos // El] += loads[e]
+    assert spread.max() <= contiguous.max()
+    layers = [EPLayer(cfg, store, DEV, 3, W, r, expert_source=store.device_expert, placement=placement)
+              for r in range(W)]
+    for r in (0, 5):
+        lay = layers[r]
+        for el in (0, El - 1):
+            e = lay.owned[el]
+            assert placement[e] == r * El + el
+            slot = lay.bank.slot_of_host[el + 1]
+            want = store.device_expert(3, e)["gate_proj"][0]
+            assert torch.equal(lay.bank.w["gate_proj"][slot].view(torch.uint8), want.view(torch.uint8))
+    outs = emulate_step(layers, xs)
+    gt = GPUTransfer(cfg, store, DEV)
+    for r in range(W):
+        single = moe_block(xs[r], 3, store, gt, cfg)
+        assert O.rel_rms(outs[r].float().cpu(), single.float().cpu()) < 5e-3
+
+
 def test_ep_full_dims_w8():
     cfg = DeepSeekConfig()
     store = SyntheticWeightStore(cfg, seed=41, device=DEV, pin_memory=False, gen_device="cuda")
