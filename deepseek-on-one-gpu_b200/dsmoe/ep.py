@@ -1,8 +1,10 @@
 """Expert parallelism for the MoE block (no counterpart in the single-GPU
 reference; the same arithmetic as ``inference/forward.py:112-153``).
 
-W ranks, rank r owns routed experts ``[r*El, (r+1)*El)`` (``El = E / W``); the
-gate and the shared expert are replicated, tokens stay on their rank. One
+W ranks, rank r owns routed experts ``[r*El, (r+1)*El)`` (``El = E / W``), or
+the experts an expert placement gives it (``EPLayer.set_placement``,
+``balanced_placement`` for skewed routing); the gate and the shared expert are
+replicated, tokens stay on their rank. One
 layer step (``EPLayer.forward``):
 
   1. route the rank's tokens (``dsmoe_route``);
