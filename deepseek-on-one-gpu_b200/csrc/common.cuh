@@ -91,6 +91,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Bounded wait used before a CTA frees what asynchronous work still uses:
+// the copies a producer issued must land in shared memory, and the MMAs an
+// issuer started must finish with TMEM, even when another role has already
+// asked every role to stop (the abort flag). So it ignores that flag and
+// gives up only after DSMOE_WAIT_NS, recording `code` (if nothing was
+// recorded yet).
+__device__ __forceinline__ bool mbar_wait_settle(uint64_t* bar, uint32_t parity, int* status, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  uint32_t n = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++n & 63) == 0 && globaltimer() - t0 > DSMOE_WAIT_NS) {
+      atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
                                             uint64_t policy) {

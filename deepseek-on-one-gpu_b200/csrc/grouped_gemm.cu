@@ -279,11 +279,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         }
       }
       // Drain: the copies of the last issued stages must have landed before
-      // the CTA may exit (normally they were consumed already).
+      // the CTA may exit (normally they were consumed already; after an
+      // abort they may still be in flight).
       const int n_drain = issued < STAGES ? issued : STAGES;
       for (int d = 0; d < n_drain; ++d) {
         if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
-        mbar_wait(&full[stage], phase, p.status, kDevTimeoutProducer, s_abort);
+        mbar_wait_settle(&full[stage], phase, p.status, kDevTimeoutProducer);
       }
     }
   } else if (warp == 1 || warp == 2) {
@@ -336,9 +337,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_cons
         }
       }
       // All MMAs of both issuers complete before TMEM is released (the
-      // barrier's first phase needs one commit from each).
+      // barrier's first phase needs one commit from each), also after an abort.
       mma_commit(done_bar);
-      mbar_wait(done_bar, 0, p.status, kDevTimeoutMma, s_abort);
+      mbar_wait_settle(done_bar, 0, p.status, kDevTimeoutMma);
     }
   } else {
     // ------------------------------------------------------------ epilogue

@@ -84,7 +84,7 @@ router_logits_tc(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
       const int n_drain = issued < STAGES ? issued : STAGES;
       for (int i = 0; i < n_drain; ++i) {
         if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
-        mbar_wait(&full[stage], phase, status, kDevTimeoutProducer, s_abort);
+        mbar_wait_settle(&full[stage], phase, status, kDevTimeoutProducer);  // copies in flight land
       }
     }
   } else if (warp == 1) {
@@ -104,6 +104,8 @@ router_logits_tc(const __grid_constant__ CUtensorMap tm_x, const __grid_constant
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
       mma_commit(done);
+      // the MMAs finish with TMEM before it is freed, also after an abort
+      mbar_wait_settle(done, 0, status, kDevTimeoutMma);
     }
   } else {
     // epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 = tokens of the tile
