@@ -77,6 +77,18 @@ def _rank_main(rank, world, port, q):
                         results.append(rel_rms(got.float().cpu(), single.float().cpu()))
             torch.cuda.synchronize()
             results.append(float(layer.push_status()))  # 0: every pushed row fit the receive buffers
+            # experts placed by load (the same placement on both ranks, from
+            # routing counts summed over the ranks): still the single-GPU result
+            from dsmoe.ep import balanced_placement
+
+            loads = torch.bincount(layer.route(ref[1][0])[0].reshape(-1), minlength=256).double()
+            dist.all_reduce(loads)
+            layer.set_placement(balanced_placement(loads.cpu().tolist(), world))
+            for x, _, single in ref:
+                got = layer.forward(x)
+                results.append(rel_rms(got.float().cpu(), single.float().cpu()))
+            torch.cuda.synchronize()
+            results.append(float(layer.push_status()))
         finally:
             layer.close()
         dist.barrier()
