@@ -26,11 +26,18 @@ Printed JSON keys (one line, rank 0):
              hit rate
   stages_ms  per-kernel CUDA-event times, recorded by the library at its
              stage boundaries inside the timed steps
+  clocks     nvidia-smi samples inside the timed region, and sm_mhz_device:
+             the SMs' own cycle counters over the timed steps (median over
+             SMs, dsmoe_clock_probe)
 ``--impl reference`` times only that CPU path and prints its own line.
 With N > 1 (torchrun, one rank per GPU) the step is expert-parallel (config
-3: 8192 tokens per rank, each rank owning 256/N experts, token rows and
+3: 4096 tokens per rank by default, the N=1 batch, with config 3's 8192
+measured in the same run as ``config3_t8192``; each rank owning 256/N experts, token rows and
 partial sums exchanged over peer memory; ``--nccl-exchange`` for the NCCL
-all-to-all, ``--mode replica`` for independent replicas); weak scaling.
+all-to-all, ``--mode replica`` for independent replicas); weak scaling. When
+the step's routing would load the busiest rank more than 1.25x the mean
+(config 4's skew), the experts are placed over the ranks by load
+(``--ep-placement``); the roofline and stage times are the critical rank's.
 """
 from __future__ import annotations
 
