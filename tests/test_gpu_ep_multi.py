@@ -54,12 +54,13 @@ def _rank_main(rank, world, port, q):
             results.append(rel_rms(out.float().cpu(), single.float().cpu()))
         # The same steps through the peer-memory exchange. Its expert GEMMs
         # choose their token tile from the capacity bound (2 ranks x cap = 512
-        # rows -> the 160-token tile, which sums the hi and lo activation
-        # terms in one accumulator), the all-to-all step's from the rows it
-        # received (the 32- to 128-token tiles keep the two terms in separate
-        # accumulator columns). At T=200 a rank receives ~390 rows, the same
-        # tile, so the outputs must be bit-identical; at T=64 and T=1 they may
-        # round differently and are held to the single-GPU block's tolerance.
+        # rows), the all-to-all step's from the rows it received; the
+        # 160-token tile sums the hi and lo activation terms in one
+        # accumulator, the narrower tiles keep them in separate columns, so
+        # the two steps round alike only when both land on the same side of
+        # that line. At T=200 a rank receives ~390 rows and both steps take
+        # the same tile, so the outputs must be bit-identical; T=64 and T=1
+        # are held to the single-GPU block's tolerance.
         ref = []
         for step, T in enumerate((64, 200, 1)):
             x = activations(500 + step + 10 * rank, T, 512).to(dev)
