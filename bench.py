@@ -837,11 +837,14 @@ def main():
                 step(xd)
             torch.cuda.synchronize()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            probe_d = ClockProbe(dev)
+            probe_d.start()
             a.record()
             for i in range(n_d):
                 set_profile_events(ev_d[i])
                 step(xd)
             b.record()
+            probe_d.stop()
             torch.cuda.synchronize()
             set_profile_events(None)
             ms_d = a.elapsed_time(b) / n_d
@@ -857,7 +860,7 @@ def main():
                 "gate_up_hbm_frac": gu_b / (st[2] / 1e3) / 1e9 / hbm_peak,
                 "down_hbm_frac": dn_b / (st[4] / 1e3) / 1e9 / hbm_peak,
                 "step_hbm_frac": (gu_b + dn_b) / (ms_d / 1e3) / 1e9 / hbm_peak,
-                "algorithmic_bytes_gemms": gu_b + dn_b}
+                "algorithmic_bytes_gemms": gu_b + dn_b, "sm_mhz_device": probe_d.mhz()}
         decode["note"] = ("hbm fractions: algorithmic bytes (weights of the experts touched + activation rows in "
                           "and out) / CUDA-event time, of measured HBM " + f"{hbm_peak:.0f} GB/s")
 
